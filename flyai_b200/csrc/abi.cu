@@ -6,6 +6,7 @@
 #include "common.cuh"
 #include "fp8_moe.cuh"
 #include "route.cuh"
+#include "tc_bank.cuh"
 
 namespace flyai {
 
@@ -38,6 +39,9 @@ static int check_desc(const flyai_moe_desc* d) {
   if (d->format == FLYAI_FMT_MXFP4) {
     if (d->gating != FLYAI_GATE_SOFTMAX_TOPK) return FLYAI_ERR_UNSUPPORTED;
     if (d->activation != FLYAI_ACT_GPTOSS_SWIGLU) return FLYAI_ERR_UNSUPPORTED;
+    // the tcgen05 kernels: K-tiles of 64, one tensor-memory accumulator row block
+    if (d->hidden % 64 || d->inter % 64) return FLYAI_ERR_ALIGNMENT;
+    if (d->hidden > kTcMaxK || d->inter > kTcMaxK) return FLYAI_ERR_UNSUPPORTED;
     if (d->n_group != 0 || d->topk_group != 0 || d->route_scale != 0.f || d->n_shared != 0)
       return FLYAI_ERR_INVALID_ARG;
     if (!(d->swiglu_limit > 0.f) || !(d->swiglu_alpha > 0.f)) return FLYAI_ERR_INVALID_ARG;
@@ -133,17 +137,15 @@ static int launch_layer_route(const flyai_moe_desc& d, int M, const void* x,
   return launch_fp8_route(d, M, x, w, logits, topk_ids, topk_weights, fw, s);
 }
 
-// Expert projections: the tcgen05 block-scaled kernels for every descriptor they
-// support (the bank was packed in their layout), else the mma.sync kernels.
+// Expert projections: the tcgen05 block-scaled kernels (every MXFP4 descriptor
+// check_desc accepts; the bank was packed in their layout).
 static int launch_experts(const flyai_moe_desc& d, int M, const void* x, bool x_split,
                           const flyai_moe_weights& w, uint16_t* pair_out, bool zero_pairs,
                           const Workspace& ws, cudaStream_t s, void* y_fold = nullptr,
                           bool* folded = nullptr) {
   const cudaEvent_t e0 = g_prof_start.load(), e1 = g_prof_stop.load();
   if (e0 && e1 && cudaEventRecord(e0, s) != cudaSuccess) return FLYAI_ERR_CUDA;
-  const int st = tc_supported(d)
-                     ? launch_tc_experts(d, M, x, x_split, w, pair_out, zero_pairs, ws, s, y_fold, folded)
-                     : launch_mxfp4_experts(d, M, x, w, pair_out, zero_pairs, ws, s, y_fold, folded);
+  const int st = launch_tc_experts(d, M, x, x_split, w, pair_out, zero_pairs, ws, s, y_fold, folded);
   if (st == FLYAI_OK && e0 && e1 && cudaEventRecord(e1, s) != cudaSuccess) return FLYAI_ERR_CUDA;
   return st;
 }
@@ -190,8 +192,7 @@ int flyai_moe_packed_bytes(const flyai_moe_desc* desc, int32_t proj, size_t* byt
   if (!bytes || (proj != FLYAI_PROJ_W13 && proj != FLYAI_PROJ_W2)) return FLYAI_ERR_INVALID_ARG;
   *bytes = desc->format == FLYAI_FMT_NVFP4 ? nv4_packed_bytes(*desc, proj)
            : is_fp8(*desc)                 ? fp8_packed_bytes(*desc, proj)
-           : tc_supported(*desc)           ? tc_packed_bytes(*desc, proj)
-                                           : mxfp4_packed_bytes(*desc, proj);
+                                           : tc_packed_bytes(*desc, proj);
   return FLYAI_OK;
 }
 
@@ -203,10 +204,7 @@ int flyai_moe_pack_mxfp4(const flyai_moe_desc* desc, int32_t proj, const void* b
   if (desc->expert_end == desc->expert_begin) return FLYAI_OK;
   if (!blocks || !scales || !packed) return FLYAI_ERR_INVALID_ARG;
   if (!aligned(blocks, 16) || !aligned(packed, 16)) return FLYAI_ERR_ALIGNMENT;
-  if (tc_supported(*desc))
-    return launch_tc_pack(*desc, proj, blocks, scales, packed, static_cast<cudaStream_t>(stream));
-  return launch_mxfp4_pack(*desc, proj, blocks, scales, packed,
-                           static_cast<cudaStream_t>(stream));
+  return launch_tc_pack(*desc, proj, blocks, scales, packed, static_cast<cudaStream_t>(stream));
 }
 
 int flyai_moe_pack_fp8(const flyai_moe_desc* desc, int32_t proj, const void* weight,
@@ -413,12 +411,12 @@ static size_t ep_rows_bytes(const flyai_moe_desc& d) {
 int flyai_moe_ep_mailbox_bytes(const flyai_moe_desc* desc, size_t* bytes) {
   FLYAI_TRY(check_desc(desc));
   if (!bytes) return FLYAI_ERR_INVALID_ARG;
-  *bytes = 256 + 2 * ep_rows_bytes(*desc);
+  *bytes = kEpFlagBytes + 2 * ep_rows_bytes(*desc);
   return FLYAI_OK;
 }
 
 int flyai_moe_ep_alloc(size_t bytes, void** mailbox) {
-  if (!mailbox || bytes < 256) return FLYAI_ERR_INVALID_ARG;
+  if (!mailbox || bytes < static_cast<size_t>(kEpFlagBytes)) return FLYAI_ERR_INVALID_ARG;
   if (cudaMalloc(mailbox, bytes) != cudaSuccess) return FLYAI_ERR_CUDA;
   if (cudaMemset(*mailbox, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
     cudaFree(*mailbox);
@@ -461,7 +459,7 @@ static int check_ep(const flyai_moe_desc* desc, int32_t M, const flyai_moe_ep_pe
   for (int r = 0; r < ep->world; ++r)
     if (!ep->mailbox[r] || !aligned(ep->mailbox[r], 256)) return FLYAI_ERR_INVALID_ARG;
   // peer-memory exchange exists for the MXFP4 tcgen05 verify kernel only
-  if (is_fp8(*desc) || !tc_supported(*desc) || M >= kTcPrefillMinTokens) return FLYAI_ERR_UNSUPPORTED;
+  if (is_fp8(*desc) || M >= kTcPrefillMinTokens) return FLYAI_ERR_UNSUPPORTED;
   return FLYAI_OK;
 }
 

@@ -207,7 +207,13 @@ __device__ __forceinline__ uint32_t lds32(const void* p) {
 // Error bits a kernel can leave in the workspace (read back with flyai_moe_read_error).
 constexpr int32_t kErrWaitTimeout = 1;
 
-constexpr int kTokChunk = 8;     // tokens of one expert per streamed pass, mma.sync kernels (mma N)
+// Expert-parallel mailbox (flyai_moe_ep_alloc): kEpFlagBytes of flag words, then
+// the pair-row buffers.  Word r = the last epoch rank r finished; word
+// kEpFailWord + r = the last epoch whose expert kernel on rank r gave up on a
+// bounded wait (its rows are incomplete).
+constexpr int kEpFlagBytes = 256;
+constexpr int kEpFailWord = 16;
+
 constexpr int kTcChunk = 4;      // tokens of one expert per chunk, tcgen05 verify kernel
 constexpr int kTcPrefillChunk = 16;   // tokens per chunk, tcgen05 prefill kernel
 constexpr int kTcPrefillMinTokens = 65;   // batches this large take the prefill kernel
@@ -243,10 +249,11 @@ struct Workspace {
   uint16_t* pair_out;  // [M*k, H] bf16 weighted expert outputs, flat pair order
   int32_t* err;        // [1] error bits set by kernels (kErr*)
   int32_t* dbg;        // [8] first failure details of the self-checking build
-  int32_t* route_ticket; // [1 + 64 + 1] at offset 0: tokens the fused route kernel
+  int32_t* route_ticket; // [1 + 64 + 2] at offset 0: tokens the fused route kernel
                          //     finished, per token its logit CTAs that finished, then
-                         //     CTAs of the expert-parallel expert kernel that finished;
-                         //     must be 0 before first use, restored to 0 by every call
+                         //     CTAs of the expert-parallel expert kernel that finished
+                         //     and whether one of them gave up on a wait; must be 0
+                         //     before first use, restored to 0 by every call
   int32_t* fold_ticket;  // [M * H/16] contributions per (token, 16-row output tile);
                          //     cleared by the route step of every call
   int32_t* n_chunks;   // [1] number of chunks (kTokChunk or kTcChunk tokens) over all non-empty experts
@@ -282,7 +289,7 @@ inline Workspace carve_workspace(const flyai_moe_desc& d, int M, void* base) {
   // The route ticket sits at offset 0 whatever the descriptor, so a workspace
   // (or the no-allocation scratch array) reused with another descriptor still
   // finds it where the previous call restored it to zero.
-  w.route_ticket = reinterpret_cast<int32_t*>(take(4 * (1 + 64 + 1)));
+  w.route_ticket = reinterpret_cast<int32_t*>(take(4 * (1 + 64 + 2)));
   w.logits = reinterpret_cast<float*>(take(static_cast<size_t>(M) * E * 4));
   w.ids = reinterpret_cast<int32_t*>(take(P * 4));
   w.wts = reinterpret_cast<float*>(take(P * 4));

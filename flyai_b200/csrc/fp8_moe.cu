@@ -30,6 +30,7 @@
 #include "fp8_moe.cuh"
 #include "tc_bank.cuh"
 #include "tcgen05.cuh"
+#include "torch_topk.cuh"
 
 namespace flyai {
 
@@ -205,9 +206,34 @@ __device__ __forceinline__ void f8_quant_block(const uint16_t* src, uint8_t* q, 
   if (lane == 0) *sc = s;
 }
 
+// Per-warp selection scratch: torch_topk_warp's, then 32 (value, index) pairs
+// for the group scores.
+constexpr int kF8SelScratch = kTopkWarpScratch + 32 * static_cast<int>(sizeof(KV));
+
+// The groups torch.topk(group_scores, topk_group, sorted=False) keeps -- a set,
+// but with tied scores at the boundary which group wins is decided by torch's
+// selection order, so it is computed by the restatement (one lane, n_group <= 32
+// pairs).  Lanes with holder set pass group g's score; all lanes get the mask.
+__device__ uint32_t f8_keep_groups(float gs, int g, bool holder, int n_group, int topk_group,
+                                   void* tks) {
+  KV* gk = reinterpret_cast<KV*>(static_cast<char*>(tks) + kTopkWarpScratch);
+  __syncwarp();
+  if (holder) gk[g] = KV{gs, g};
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) torch_topk_serial(gk, n_group, topk_group, false);
+  __syncwarp();
+  uint32_t keep = 0;
+  for (int r = 0; r < topk_group; ++r) keep |= 1u << gk[r].i;
+  __syncwarp();
+  return keep;
+}
+
 // Experts of token t, one warp.  Lane l holds experts l*nj .. l*nj+nj-1; row is
-// a warp-private E-float shared buffer for the group scores.
-__device__ void f8_select_token(const F8RouteParams& p, int t, float* row) {
+// a warp-private shared buffer of E (value, index) pairs (group scores, then the
+// top-k), tks the warp's torch_topk_warp scratch.  The ids come out in the order
+// torch.topk(sorted=False) returns them on CPU (torch_topk.cuh); the weights are
+// renormalised in that slot order, as the reference sums them.
+__device__ void f8_select_token(const F8RouteParams& p, int t, KV* row, void* tks) {
   const int lane = threadIdx.x & 31, E = p.E, nj = E >> 5, k = p.k;
   float sc[16], ch[16];
 #pragma unroll
@@ -220,7 +246,7 @@ __device__ void f8_select_token(const F8RouteParams& p, int t, float* row) {
       const float s = __frcp_rn(__fadd_rn(1.f, expf(-l)));
       sc[j] = s;
       ch[j] = __fadd_rn(s, __ldg(p.bias + e));
-      row[e] = ch[j];
+      row[e].v = ch[j];
     }
   }
   __syncwarp();
@@ -231,7 +257,7 @@ __device__ void f8_select_token(const F8RouteParams& p, int t, float* row) {
     if (lane < p.n_group) {
       float m1 = -INFINITY, m2 = -INFINITY;
       for (int i = 0; i < gsize; ++i) {
-        const float v = row[lane * gsize + i];
+        const float v = row[lane * gsize + i].v;
         if (v > m1) {
           m2 = m1;
           m1 = v;
@@ -241,58 +267,28 @@ __device__ void f8_select_token(const F8RouteParams& p, int t, float* row) {
       }
       gs = __fadd_rn(m1, m2);
     }
-    uint32_t keep = 0;
-    for (int r = 0; r < p.topk_group; ++r) {
-      float bv = (lane < p.n_group && !((keep >> lane) & 1u)) ? gs : -INFINITY;
-      int bg = (lane < p.n_group && !((keep >> lane) & 1u)) ? lane : 32;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int og = __shfl_xor_sync(0xffffffffu, bg, o);
-        if (ov > bv || (ov == bv && og < bg)) {
-          bv = ov;
-          bg = og;
-        }
-      }
-      if (bg < 32) keep |= 1u << bg;
-    }
+    const uint32_t keep = f8_keep_groups(gs, lane, lane < p.n_group, p.n_group, p.topk_group, tks);
 #pragma unroll
     for (int j = 0; j < 16; ++j)
       if (j < nj && !((keep >> ((lane * nj + j) / gsize)) & 1u)) ch[j] = -INFINITY;
   }
-  uint32_t taken = 0;
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    if (j < nj) row[lane * nj + j] = KV{ch[j], lane * nj + j};
+  torch_topk_warp(row, E, k, tks);
   int my_id = 0;
   float my_w = 0.f;
   for (int r = 0; r < k; ++r) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int e = lane * nj + j;
-      if (j < nj && !((taken >> j) & 1u) && (ch[j] > bv || (ch[j] == bv && e < bi))) {
-        bv = ch[j];
-        bi = e;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if (bi >= E) bi = r;   // only reachable with NaN scores
-    const int owner = bi / nj, jj = bi - owner * nj;
+    const int id = row[r].i;
+    const int owner = id / nj, jj = id - owner * nj;
     float s_sel = 0.f;
 #pragma unroll
     for (int j = 0; j < 16; ++j)
       if (j == jj) s_sel = sc[j];
     s_sel = __shfl_sync(0xffffffffu, s_sel, owner);
-    if (lane == owner) taken |= 1u << jj;
     if (lane == r) {
-      my_id = bi;
+      my_id = id;
       my_w = s_sel;
     }
   }
@@ -316,8 +312,9 @@ __device__ void f8_select_token(const F8RouteParams& p, int t, float* row) {
 // load as two float4 each of logits and bias; groups whose size is a multiple
 // of 8 (a power-of-two number of lanes) get their top-2 sums by shuffles within
 // the lane group; the top-k pops the heads of per-lane lists sorted once by an
-// odd-even merge network.  Same selection rule (value, then lower index).
-__device__ void f8_select_token_256(const F8RouteParams& p, int t, float* row) {
+// odd-even merge network.  The top-k then comes from torch_topk_warp, in torch's
+// sorted=False order, as in f8_select_token.
+__device__ void f8_select_token_256(const F8RouteParams& p, int t, KV* row, void* tks) {
   const int lane = threadIdx.x & 31, k = p.k;
   const float4* lg = reinterpret_cast<const float4*>(p.logits + static_cast<size_t>(t) * 256 + lane * 8);
   const float4* bs = reinterpret_cast<const float4*>(p.bias + lane * 8);
@@ -353,35 +350,20 @@ __device__ void f8_select_token_256(const F8RouteParams& p, int t, float* row) {
       const float gs = __fadd_rn(m1, m2);
       const int my_g = lane / lpg;
       const bool leader = (lane % lpg) == 0;
-      uint32_t keep = 0;
-      for (int r = 0; r < p.topk_group; ++r) {
-        const bool live = leader && !((keep >> my_g) & 1u);
-        float v = live ? gs : -INFINITY;
-        int g = live ? my_g : 32;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-          const int og = __shfl_xor_sync(0xffffffffu, g, o);
-          if (ov > v || (ov == v && og < g)) {
-            v = ov;
-            g = og;
-          }
-        }
-        if (g < 32) keep |= 1u << g;
-      }
+      const uint32_t keep = f8_keep_groups(gs, my_g, leader, p.n_group, p.topk_group, tks);
       if (!((keep >> my_g) & 1u)) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) ch[j] = -INFINITY;
       }
     } else {   // other group sizes: group scores from a shared-memory row
 #pragma unroll
-      for (int j = 0; j < 8; ++j) row[lane * 8 + j] = ch[j];
+      for (int j = 0; j < 8; ++j) row[lane * 8 + j].v = ch[j];
       __syncwarp();
       float gsc = -INFINITY;
       if (lane < p.n_group) {
         float m1 = -INFINITY, m2 = -INFINITY;
         for (int i = 0; i < gsize; ++i) {
-          const float v = row[lane * gsize + i];
+          const float v = row[lane * gsize + i].v;
           if (v > m1) {
             m2 = m1;
             m1 = v;
@@ -391,81 +373,28 @@ __device__ void f8_select_token_256(const F8RouteParams& p, int t, float* row) {
         }
         gsc = __fadd_rn(m1, m2);
       }
-      uint32_t keep = 0;
-      for (int r = 0; r < p.topk_group; ++r) {
-        float v = (lane < p.n_group && !((keep >> lane) & 1u)) ? gsc : -INFINITY;
-        int g = (lane < p.n_group && !((keep >> lane) & 1u)) ? lane : 32;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-          const int og = __shfl_xor_sync(0xffffffffu, g, o);
-          if (ov > v || (ov == v && og < g)) {
-            v = ov;
-            g = og;
-          }
-        }
-        if (g < 32) keep |= 1u << g;
-      }
+      const uint32_t keep = f8_keep_groups(gsc, lane, lane < p.n_group, p.n_group, p.topk_group, tks);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
         if (!((keep >> ((lane * 8 + j) / gsize)) & 1u)) ch[j] = -INFINITY;
     }
   }
-  // this lane's candidates sorted once (value descending, index ascending)
-  float v[8];
-  int ix[8];
+  __syncwarp();
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    v[j] = ch[j];
-    ix[j] = lane * 8 + j;
-  }
-  constexpr int kNet[19][2] = {{0, 1}, {2, 3}, {4, 5}, {6, 7}, {0, 2}, {1, 3}, {4, 6},
-                               {5, 7}, {1, 2}, {5, 6}, {0, 4}, {3, 7}, {1, 5}, {2, 6},
-                               {1, 4}, {3, 6}, {2, 4}, {3, 5}, {3, 4}};
-#pragma unroll
-  for (int c = 0; c < 19; ++c) {
-    const int a = kNet[c][0], b = kNet[c][1];
-    if (v[b] > v[a] || (v[b] == v[a] && ix[b] < ix[a])) {
-      const float tv = v[a];
-      v[a] = v[b];
-      v[b] = tv;
-      const int ti = ix[a];
-      ix[a] = ix[b];
-      ix[b] = ti;
-    }
-  }
+  for (int j = 0; j < 8; ++j) row[lane * 8 + j] = KV{ch[j], lane * 8 + j};
+  torch_topk_warp(row, 256, k, tks);
   int my_id = 0;
   float my_w = 0.f;
   for (int r = 0; r < k; ++r) {
-    float wv = v[0];
-    int wi = ix[0];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, wv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, wi, o);
-      if (ov > wv || (ov == wv && oi < wi)) {
-        wv = ov;
-        wi = oi;
-      }
-    }
-    if (wi >= 256) wi = r;   // only reachable with NaN scores
-    const int owner = wi >> 3, jj = wi & 7;
+    const int id = row[r].i;
+    const int owner = id >> 3, jj = id & 7;
     float s_sel = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j)
       if (j == jj) s_sel = sc[j];
     s_sel = __shfl_sync(0xffffffffu, s_sel, owner);
-    if (lane == owner && ix[0] == wi) {   // pop the head
-#pragma unroll
-      for (int j = 0; j < 7; ++j) {
-        v[j] = v[j + 1];
-        ix[j] = ix[j + 1];
-      }
-      v[7] = -INFINITY;
-      ix[7] = 0x7fffffff;
-    }
     if (lane == r) {
-      my_id = wi;
+      my_id = id;
       my_w = s_sel;
     }
   }
@@ -490,7 +419,8 @@ __global__ void __launch_bounds__(kF8RouteThreads, kNv ? 1 : 2) f8_route_kernel(
   __shared__ float rowmax[kF8RouteTokens][8];   // NVFP4: |x| maximum per token and K slice
   __shared__ int32_t ids_s[kF8MaxTokens * kMaxTopK];
   __shared__ int32_t off_s[kF8MaxExperts];
-  __shared__ __align__(16) int32_t scratch[16 * kF8MaxExperts];   // choice rows, then warp histograms
+  __shared__ __align__(16) int32_t scratch[16 * kF8MaxExperts];   // choice rows (KV), then warp histograms
+  __shared__ __align__(16) uint8_t tk_s[8][kF8SelScratch];
   __shared__ int scan_tmp[33];
   __shared__ int last_s;
   pdl_wait();
@@ -631,10 +561,10 @@ __global__ void __launch_bounds__(kF8RouteThreads, kNv ? 1 : 2) f8_route_kernel(
   __threadfence();
 
   // ---- this token group's experts ----
-  float* rows = reinterpret_cast<float*>(scratch);
+  KV* rows = reinterpret_cast<KV*>(scratch);
   if (warp < nt) {
-    if (E == 256) f8_select_token_256(p, t0 + warp, rows + warp * E);
-    else f8_select_token(p, t0 + warp, rows + warp * E);
+    if (E == 256) f8_select_token_256(p, t0 + warp, rows + warp * E, tk_s[warp]);
+    else f8_select_token(p, t0 + warp, rows + warp * E, tk_s[warp]);
   }
   if (gridDim.y > 1) {   // (one token group: this CTA is the last one already)
     __threadfence();
@@ -774,13 +704,14 @@ int launch_fp8_route(const flyai_moe_desc& d, int M, const void* x, const flyai_
 // Prefill-size batches: the selection as a launch of its own (one warp per
 // token) on the logits ws.logits already holds (nv4_prefill.cu computes them).
 __global__ void __launch_bounds__(256) f8_select_kernel(const __grid_constant__ F8RouteParams p) {
-  __shared__ __align__(16) float rows[8 * kF8MaxExperts];
+  __shared__ __align__(16) KV rows[8 * kF8MaxExperts];
+  __shared__ __align__(16) uint8_t tk_s[8][kF8SelScratch];
   pdl_wait();
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, t = blockIdx.x * 8 + warp;
   if (t >= p.M) return;   // whole warps
-  if (p.E == 256) f8_select_token_256(p, t, rows + warp * p.E);
-  else f8_select_token(p, t, rows + warp * p.E);
+  if (p.E == 256) f8_select_token_256(p, t, rows + warp * p.E, tk_s[warp]);
+  else f8_select_token(p, t, rows + warp * p.E, tk_s[warp]);
 }
 
 int launch_fp8_select(const flyai_moe_desc& d, int M, const flyai_moe_weights& w,

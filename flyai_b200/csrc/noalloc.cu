@@ -23,9 +23,18 @@
 //     region before reading it, and the one region that must start at zero (the
 //     pair rows of other shards' experts under a partial expert range) is
 //     cleared by the call itself.
-//   * The first call on a device looks up the array's device address with
-//     cudaGetSymbolAddress and caches it; make that first call before capturing
-//     the stream into a CUDA graph.
+//   * The array's device address belongs to a CUDA context.  Every call made
+//     outside stream capture looks it up again (cudaGetSymbolAddress) for the
+//     context current on the calling thread and records it per context; a call
+//     issued while its stream is being captured into a CUDA graph uses the
+//     recorded address, so make one call on that context before capturing.  A
+//     context that was destroyed and recreated (cudaDeviceReset, or a host that
+//     manages its own contexts) gets its own lookup on its first uncaptured call.
+//   * Error bits that kernels record (a bounded wait that gave up) land in the
+//     array, where no caller can read them: flyai_moe_read_error needs a
+//     workspace pointer.  On this path a call that hit such a wait returns
+//     FLYAI_OK with a zero output; callers that must observe it use
+//     flyai_moe_forward with their own workspace.
 #include <mutex>
 
 #include "common.cuh"
@@ -39,24 +48,64 @@ namespace flyai {
 static __device__ __align__(256) unsigned char g_noalloc_scratch[FLYAI_MOE_NOALLOC_SCRATCH_BYTES];
 
 namespace {
-constexpr int kMaxDevices = 64;
+constexpr int kMaxContexts = 64;
+struct CtxAddr {
+  void* ctx;
+  void* addr;
+};
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kMaxDevices] = {};
+CtxAddr g_noalloc_cache[kMaxContexts] = {};
+int g_noalloc_next = 0;
+
+// cuCtxGetCurrent through the runtime's driver entry point table (the library
+// links the static runtime, not libcuda, directly).
+using CtxGetCurrentFn = int (*)(void**);
+CtxGetCurrentFn ctx_get_current() {
+  static const CtxGetCurrentFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<CtxGetCurrentFn>(nullptr);
+    return reinterpret_cast<CtxGetCurrentFn>(f);
+  }();
+  return fn;
+}
 }  // namespace
 
-// Host-side address of this device's scratch array (the symbol itself is only
-// a host stand-in, not a device address).  Looked up once per device.
-static int noalloc_scratch(void** out) {
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FLYAI_ERR_CUDA;
+// Device address of the scratch array in the calling thread's current context
+// (the symbol itself is only a host stand-in, not a device address).
+static int noalloc_scratch(cudaStream_t stream, void** out) {
+  const CtxGetCurrentFn get_ctx = ctx_get_current();
+  void* ctx = nullptr;
+  if (!get_ctx || get_ctx(&ctx) != 0) return FLYAI_ERR_CUDA;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  const bool capturing = cudaStreamIsCapturing(stream, &cs) != cudaSuccess ||
+                         cs != cudaStreamCaptureStatusNone;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
-      return FLYAI_ERR_CUDA;
-    g_noalloc_ptr[dev] = p;
+  int slot = -1;
+  if (ctx)
+    for (int i = 0; i < kMaxContexts; ++i)
+      if (g_noalloc_cache[i].ctx == ctx) slot = i;
+  if (capturing) {
+    if (slot < 0) return FLYAI_ERR_CUDA;   // no uncaptured call on this context yet
+    *out = g_noalloc_cache[slot].addr;
+    return FLYAI_OK;
   }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
+    return FLYAI_ERR_CUDA;
+  if (!ctx) {   // the lookup made the runtime's primary context current
+    if (get_ctx(&ctx) != 0 || !ctx) return FLYAI_ERR_CUDA;
+    for (int i = 0; i < kMaxContexts; ++i)
+      if (g_noalloc_cache[i].ctx == ctx) slot = i;
+  }
+  if (slot < 0) {
+    slot = g_noalloc_next;
+    g_noalloc_next = (g_noalloc_next + 1) % kMaxContexts;
+  }
+  g_noalloc_cache[slot] = CtxAddr{ctx, p};
+  *out = p;
   return FLYAI_OK;
 }
 
@@ -74,7 +123,7 @@ extern "C" int flyai_moe_forward_noalloc(const flyai_moe_desc* desc, int32_t M, 
   if (flyai_moe_workspace_bytes(desc, &need) != FLYAI_OK) return FLYAI_ERR_INVALID_ARG;
   if (need > FLYAI_MOE_NOALLOC_SCRATCH_BYTES) return FLYAI_ERR_WORKSPACE;
   void* scratch = nullptr;
-  const int sst = noalloc_scratch(&scratch);
+  const int sst = noalloc_scratch(static_cast<cudaStream_t>(stream), &scratch);
   if (sst != FLYAI_OK) return sst;
   // Same validation and launch sequence as flyai_moe_forward, on the static array.
   return flyai_moe_forward(desc, M, x, w, y, topk_ids, topk_weights, scratch,

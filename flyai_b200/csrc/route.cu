@@ -8,6 +8,7 @@
 #include "common.cuh"
 #include "route.cuh"
 #include "terms.cuh"
+#include "torch_topk.cuh"
 
 namespace flyai {
 
@@ -66,158 +67,15 @@ __global__ void __launch_bounds__(256) route_logits_kernel(const uint16_t* __res
 }
 
 // ---------------------------------------------------------------------------
-// 2) torch CPU topk, restated.  torch (aten/src/ATen/native/cpu/SortingKernel.cpp
-// topk_impl_loop) runs std::nth_element(q, q+k-1, q+n, greater) and then
-// std::sort(q, q+k-1, greater) when 64*k > n (else std::partial_sort); among
-// equal values the result is whatever libstdc++'s introselect leaves, so the
-// device code below is a step-for-step restatement of libstdc++'s published
-// __introselect / __unguarded_partition_pivot / __insertion_sort / heap
-// routines, run by one lane on a shared-memory copy of the row.
+// 2) torch CPU topk (sorted=True for GPT-OSS), via torch_topk.cuh's
+// restatement of libstdc++'s selection, run by one lane on a shared-memory copy
+// of the row when the fast path below cannot decide.
 // ---------------------------------------------------------------------------
-struct KV {
-  float v;
-  int i;
-};
-
-__device__ __forceinline__ bool kv_gt(const KV& x, const KV& y) {
-  return (isnan(x.v) && !isnan(y.v)) || x.v > y.v;
-}
-
-__device__ void kv_insertion_sort(KV* a, int f, int l) {
-  if (f == l) return;
-  for (int i = f + 1; i < l; ++i) {
-    KV v = a[i];
-    if (kv_gt(v, a[f])) {
-      for (int j = i; j > f; --j) a[j] = a[j - 1];
-      a[f] = v;
-    } else {
-      int j = i, n = i - 1;
-      while (kv_gt(v, a[n])) {
-        a[j] = a[n];
-        j = n;
-        --n;
-      }
-      a[j] = v;
-    }
-  }
-}
-
-__device__ __forceinline__ void kv_swap(KV* a, int i, int j) {
-  KV t = a[i];
-  a[i] = a[j];
-  a[j] = t;
-}
-
-__device__ void kv_move_median_to_first(KV* a, int r, int x, int y, int z) {
-  if (kv_gt(a[x], a[y])) {
-    if (kv_gt(a[y], a[z])) kv_swap(a, r, y);
-    else if (kv_gt(a[x], a[z])) kv_swap(a, r, z);
-    else kv_swap(a, r, x);
-  } else if (kv_gt(a[x], a[z])) {
-    kv_swap(a, r, x);
-  } else if (kv_gt(a[y], a[z])) {
-    kv_swap(a, r, z);
-  } else {
-    kv_swap(a, r, y);
-  }
-}
-
-__device__ int kv_unguarded_partition(KV* a, int f, int l, int p) {
-  while (true) {
-    while (kv_gt(a[f], a[p])) ++f;
-    --l;
-    while (kv_gt(a[p], a[l])) --l;
-    if (!(f < l)) return f;
-    kv_swap(a, f, l);
-    ++f;
-  }
-}
-
-__device__ void kv_adjust_heap(KV* a, int first, int hole, int len, KV value) {
-  const int top = hole;
-  int second = hole;
-  while (second < (len - 1) / 2) {
-    second = 2 * (second + 1);
-    if (kv_gt(a[first + second], a[first + second - 1])) --second;
-    a[first + hole] = a[first + second];
-    hole = second;
-  }
-  if ((len & 1) == 0 && second == (len - 2) / 2) {
-    second = 2 * (second + 1);
-    a[first + hole] = a[first + second - 1];
-    hole = second - 1;
-  }
-  int parent = (hole - 1) / 2;
-  while (hole > top && kv_gt(a[first + parent], value)) {
-    a[first + hole] = a[first + parent];
-    hole = parent;
-    parent = (hole - 1) / 2;
-  }
-  a[first + hole] = value;
-}
-
-__device__ void kv_heap_select(KV* a, int f, int m, int l) {
-  const int n = m - f;
-  if (n >= 2) {
-    for (int parent = (n - 2) / 2;; --parent) {
-      kv_adjust_heap(a, f, parent, n, a[f + parent]);
-      if (parent == 0) break;
-    }
-  }
-  for (int i = m; i < l; ++i) {
-    if (kv_gt(a[i], a[f])) {
-      KV v = a[i];
-      a[i] = a[f];
-      kv_adjust_heap(a, f, 0, n, v);
-    }
-  }
-}
-
-__device__ void kv_sort_heap(KV* a, int f, int l) {
-  while (l - f > 1) {
-    --l;
-    KV v = a[l];
-    a[l] = a[f];
-    kv_adjust_heap(a, f, 0, l - f, v);
-  }
-}
-
-__device__ int ilog2_floor(int n) { return 31 - __clz(n); }
-
-// Leaves torch.topk(values, k, sorted)'s index order in a[0..k).
-__device__ void torch_topk_serial(KV* a, int n, int k, bool sorted) {
-  if (k * 64 <= n) {
-    kv_heap_select(a, 0, k, n);
-    kv_sort_heap(a, 0, k);
-    return;
-  }
-  int f = 0, l = n;
-  const int nth = k - 1;
-  int depth = 2 * ilog2_floor(n);
-  while (l - f > 3) {
-    if (depth == 0) {
-      kv_heap_select(a, f, nth + 1, l);
-      kv_swap(a, f, nth);
-      goto selected;
-    }
-    --depth;
-    {
-      const int mid = f + (l - f) / 2;
-      kv_move_median_to_first(a, f, f + 1, mid, l - 1);
-      const int cut = kv_unguarded_partition(a, f + 1, l, f);
-      if (cut <= nth) f = cut;
-      else l = cut;
-    }
-  }
-  kv_insertion_sort(a, f, l);
-selected:
-  if (sorted) kv_insertion_sort(a, 0, k - 1);
-}
 
 // One warp selects one token.  Fast path: when the k+1 largest values are
 // strictly decreasing (and nothing is NaN) the answer is unique -- the k
 // largest in descending order -- and is found with warp arg-max rounds.  Any
-// tie or NaN falls back to the serial libstdc++ restatement above.
+// tie or NaN falls back to the serial libstdc++ restatement (torch_topk_serial).
 __device__ void select_softmax_token(const float* __restrict__ lr, KV* row, int m, int E, int k,
                                      int32_t* __restrict__ ids, float* __restrict__ wts,
                                      int32_t* __restrict__ ids_out, uint16_t* __restrict__ wts_out) {
@@ -341,8 +199,8 @@ __device__ void route_plan_block(const int32_t* __restrict__ ids, int P, int e_b
                                  int32_t* __restrict__ chunk_slot, int32_t* __restrict__ chunk_c0,
                                  int max_chunks, int32_t* plan_smem, int k, int4* chunk_info,
                                  int32_t* chunk_rows, int32_t* chunk_done) {
-  // chunk size: the tcgen05 kernels' (chunk_info set; by batch size), else kTokChunk
-  const int ct = chunk_info ? tc_chunk_tokens(P / k) : kTokChunk;
+  // chunk size of the tcgen05 kernels (by batch size)
+  const int ct = tc_chunk_tokens(P / k);
   const int tid = threadIdx.x, nth = blockDim.x;
   const int warp = tid >> 5, lane = tid & 31, nwarps = nth >> 5;
   const int El = e_count;
@@ -508,7 +366,7 @@ __device__ void route_plan_small(const int32_t* __restrict__ ids, int P, int e_b
                                  int max_chunks, int4* chunk_info, int32_t* chunk_rows,
                                  int32_t* chunk_done, int32_t* sm) {
   const int lane = threadIdx.x & 31;
-  const int ct = chunk_info ? tc_chunk_tokens(P / k) : kTokChunk;
+  const int ct = tc_chunk_tokens(P / k);
   int32_t* ids_s = sm;              // [P] local expert or -1
   int32_t* rank_s = ids_s + P;      // [P] rank of the pair inside its expert (flat order)
   int32_t* perm_s = rank_s + P;     // [P]

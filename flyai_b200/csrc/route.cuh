@@ -7,21 +7,9 @@ int launch_route(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_
                  void* logits_out, int32_t* ids_out, void* wts_out, const Workspace& ws,
                  cudaStream_t stream);
 
-int launch_mxfp4_pack(const flyai_moe_desc& d, int proj, const void* blocks, const void* scales,
-                      void* packed, cudaStream_t stream);
-size_t mxfp4_packed_bytes(const flyai_moe_desc& d, int proj);
-
-// Routed experts of this shard -> ws.pair_out rows (flat pair order).
-// y_fold != null (single GPU, every expert local): the down kernel may also
-// fold each token's rows into y; *folded reports whether it did (otherwise the
-// caller runs launch_combine).
-int launch_mxfp4_experts(const flyai_moe_desc& d, int M, const void* x,
-                         const flyai_moe_weights& w, uint16_t* pair_out, bool zero_pairs,
-                         const Workspace& ws, cudaStream_t stream, void* y_fold = nullptr,
-                         bool* folded = nullptr);
-
-// Tensor-core (tcgen05 kind::mxf4) expert path: used for every descriptor
-// tc_supported accepts; the bank layout then is the tile layout of tc_experts.cu.
+// Tensor-core (tcgen05 kind::mxf4) expert path: every MXFP4 descriptor the ABI
+// accepts (hidden and inter multiples of 64, at most kTcMaxK); the bank layout is
+// the tile layout of tc_experts.cu.
 bool tc_supported(const flyai_moe_desc& d);
 size_t tc_packed_bytes(const flyai_moe_desc& d, int proj);
 int launch_tc_pack(const flyai_moe_desc& d, int proj, const void* blocks, const void* scales,

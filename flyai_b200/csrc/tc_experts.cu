@@ -26,12 +26,7 @@
 namespace flyai {
 
 bool tc_supported(const flyai_moe_desc& d) {
-  static const bool allowed = [] {
-    const char* v = getenv("FLYAI_MOE_KERNEL");
-    return !(v && v[0] == 'm');   // FLYAI_MOE_KERNEL=mma selects the mma.sync kernels
-  }();
-  return allowed && d.hidden % 64 == 0 && d.inter % 64 == 0 && d.hidden <= kTcMaxK &&
-         d.inter <= kTcMaxK;
+  return d.hidden % 64 == 0 && d.inter % 64 == 0 && d.hidden <= kTcMaxK && d.inter <= kTcMaxK;
 }
 
 size_t tc_packed_bytes(const flyai_moe_desc& d, int proj) {
@@ -140,21 +135,38 @@ struct TcParams {
   uint32_t ep_epoch;
   uint16_t* ep_rows[FLYAI_MOE_EP_MAX_RANKS];
   uint32_t* ep_flags[FLYAI_MOE_EP_MAX_RANKS];
-  int32_t* ep_ticket;         // CTAs that finished (workspace, self-resetting)
+  int32_t* ep_ticket;         // [0] CTAs that finished, [1] set when a wait gave up
+                              // (workspace, self-resetting)
 };
+
+// A bounded wait gave up: the error word gets kErrWaitTimeout and, under expert
+// parallelism, the call is marked failed so its peers do not fold partial rows.
+__device__ __forceinline__ void tc_record_timeout(const TcParams& p) {
+  atomicOr(p.err, kErrWaitTimeout);
+  if (p.ep_world) atomicExch(p.ep_ticket + 1, 1);
+}
 
 // The last CTA of this rank's expert kernel raises this rank's flag to the
 // call's epoch in every rank's mailbox (system-scope release after every CTA's
-// rows were made visible system-wide).
+// rows were made visible system-wide).  When any CTA of the call gave up on a
+// wait it first raises this rank's failure word to the epoch, which the peers'
+// combine turns into an error instead of a fold.
 __device__ __forceinline__ void tc_ep_signal(const TcParams& p) {
   __threadfence_system();
   if (atomicAdd(p.ep_ticket, 1) != static_cast<int>(gridDim.x) - 1) return;
   *p.ep_ticket = 0;
+  __threadfence();
+  const bool failed = atomicExch(p.ep_ticket + 1, 0) != 0;
   __threadfence_system();
-  for (int r = 0; r < p.ep_world; ++r)
+  for (int r = 0; r < p.ep_world; ++r) {
+    if (failed)
+      asm volatile("st.relaxed.sys.global.u32 [%0], %1;\n" ::"l"(p.ep_flags[r] + kEpFailWord + p.ep_rank),
+                   "r"(p.ep_epoch)
+                   : "memory");
     asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p.ep_flags[r] + p.ep_rank),
                  "r"(p.ep_epoch)
                  : "memory");
+  }
 }
 
 // Shared memory: weight ring, two B buffers (kTcChunk term rows each), one
@@ -290,7 +302,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
         const uint32_t last = ((li - 1 - s) / S) * S + s;
         if (!mbar_wait_bounded(&full[s], (last / S) & 1)) ok = false;
       }
-      if (!ok) atomicOr(p.err, kErrWaitTimeout);
+      if (!ok) tc_record_timeout(p);
     }
     __syncwarp();
   } else if (warp == 1 || warp == 7) {
@@ -390,7 +402,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
       if (!mbar_wait_bounded(&iss_done[odd], 0)) ok = false;
       // tensor memory goes back only after the epilogue read its last accumulator
       if (!odd && !mbar_wait_bounded(epi_done, 0)) ok = false;
-      if (!ok) atomicOr(p.err, kErrWaitTimeout);
+      if (!ok) tc_record_timeout(p);
       if (!odd && p.ep_world) tc_ep_signal(p);   // all of this CTA's rows are stored
     }
     __syncwarp();
@@ -425,7 +437,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
       const uint32_t buf = item_no % kTcAcc, use = item_no / kTcAcc;
       if (ok && !mbar_wait_bounded(&acc_full[buf], use & 1)) {
         ok = false;
-        atomicOr(p.err, kErrWaitTimeout);
+        tc_record_timeout(p);
       }
       tc::fence_after_sync();
       float val[kTcChunk];
@@ -581,7 +593,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
       // copies in flight land before the CTA exits
       for (uint32_t c = (bc >= 2 ? bc - 2 : 0); ok && c < bc; ++c)
         if (!mbar_wait_bounded(&b_full[c & 1], (c >> 1) & 1)) ok = false;
-      if (!ok) atomicOr(p.err, kErrWaitTimeout);
+      if (!ok) tc_record_timeout(p);
     }
     __syncwarp();
   }
@@ -675,7 +687,7 @@ int launch_tc_experts(const flyai_moe_desc& d, int M, const void* x, bool x_spli
     for (int r = 0; r < ep->world; ++r) {
       uint8_t* mb = static_cast<uint8_t*>(ep->mailbox[r]);
       prm.ep_flags[r] = reinterpret_cast<uint32_t*>(mb);
-      prm.ep_rows[r] = reinterpret_cast<uint16_t*>(mb + 256 + (ep->epoch & 1) * rows_bytes);
+      prm.ep_rows[r] = reinterpret_cast<uint16_t*>(mb + kEpFlagBytes + (ep->epoch & 1) * rows_bytes);
     }
     prm.ep_ticket = ws.route_ticket + 65;
   }

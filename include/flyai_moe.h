@@ -160,7 +160,7 @@ FLYAI_API int flyai_moe_pack_nvfp4(const flyai_moe_desc* desc, int32_t proj, con
 /* Workspace bytes for calls with up to desc->max_tokens tokens.  The layout
  * depends only on the descriptor, so one workspace serves every call with
  * num_tokens <= max_tokens.  Zero-fill a workspace once before its first use:
- * its first 264 bytes are counters the kernels keep and restore to zero after
+ * its first 268 bytes are counters the kernels keep and restore to zero after
  * every call (also when the workspace is reused with another descriptor). */
 FLYAI_API int flyai_moe_workspace_bytes(const flyai_moe_desc* desc, size_t* bytes);
 
@@ -269,9 +269,15 @@ FLYAI_API int flyai_moe_forward(const flyai_moe_desc* desc, int32_t num_tokens, 
  * the process exits; nothing is allocated.  Descriptors whose workspace
  * (flyai_moe_workspace_bytes) exceeds that size are refused with
  * FLYAI_ERR_WORKSPACE.  All calls on a device share the one array: calls that
- * overlap on the GPU race, so order them on one stream.  The first call on each
- * device looks up the array's address (cudaGetSymbolAddress); make it before
- * capturing that stream into a CUDA graph.  Same outputs as flyai_moe_forward. */
+ * overlap on the GPU race, so order them on one stream.  The array's address
+ * belongs to a CUDA context: every call outside stream capture looks it up
+ * (cudaGetSymbolAddress) for the calling thread's current context and records
+ * it; a call made while its stream is being captured uses the recorded address,
+ * so make one uncaptured call on that context first (a context destroyed and
+ * recreated, e.g. by cudaDeviceReset, needs its own).  Device error bits (a
+ * bounded wait that gave up) land in the array and cannot be read on this path:
+ * use flyai_moe_forward with a workspace and flyai_moe_read_error to observe
+ * them.  Same outputs as flyai_moe_forward. */
 #define FLYAI_MOE_NOALLOC_SCRATCH_BYTES (8u << 20)
 FLYAI_API int flyai_moe_forward_noalloc(const flyai_moe_desc* desc, int32_t num_tokens,
                                         const void* x, const flyai_moe_weights* w, void* y,

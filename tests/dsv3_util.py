@@ -80,11 +80,27 @@ def bf16_ulp(v):
     return np.exp2(np.floor(np.log2(a)) - 7)
 
 
-def assert_close(got, ref, rel_l2=5e-3, max_abs=2e-2):
+# Element-wise bounds in bf16 steps (tests.golden_util.bf16_steps), per layer.
+# DeepSeek-V3: the reference re-quantises every SwiGLU row to e4m3 per 1x128
+# block (act_quant), so a one-step bf16 difference before it (fp32 summation
+# order) can move an e4m3 code and the output by several steps; the vendored
+# reference and the numpy oracle -- the same arithmetic, another fp32 order --
+# agree within one step on 98.99 % of the full-size M=8 fixture's elements.
+# MiniMax-M2.5: bf16 chain without re-quantisation; 99.75 % on the same test.
+DSV3_ULP_FRAC1 = 0.985
+M25_ULP_FRAC1 = 0.995
+
+
+def assert_close(got, ref, rel_l2=5e-3, max_abs=2e-2, ulp_frac1=DSV3_ULP_FRAC1, ulp_max=None):
     """The layer tolerance: rel-L2 5e-3 and max-abs 2e-2 in bf16.  The max-abs bound
     scales with the output's RMS when that exceeds 1, and an element may always
-    differ by two bf16 ulps of its own size (one ulp at |y| ~ 50 is 0.25)."""
+    differ by two bf16 ulps of its own size (one ulp at |y| ~ 50 is 0.25).  On top,
+    the element-wise distance in bf16 steps: at least ulp_frac1 of the elements
+    within one step, none beyond ulp_max (None: not checked).  The returned
+    metrics carry the unscaled max-abs and the step statistics."""
+    from tests.golden_util import ulp_stats
     m = metrics(got, ref)
+    m.update(ulp_stats(got, ref))
     ref = np.asarray(ref, np.float64)
     rms = float(np.sqrt(np.mean(ref ** 2))) if ref.size else 0.0
     m["rms"] = rms
@@ -92,15 +108,26 @@ def assert_close(got, ref, rel_l2=5e-3, max_abs=2e-2):
     over = np.abs(np.asarray(got, np.float64) - ref) > bound
     m["over_bound"] = int(over.sum())
     assert not over.any() and m["rel_l2"] <= rel_l2, m
+    if ulp_frac1 is not None:
+        assert m["ulp_le1"] >= ulp_frac1, m
+    if ulp_max is not None:
+        assert m["ulp_max"] <= ulp_max, m
     return m
 
 
 def assert_same_routing(ids, wts, ref_ids, ref_wts, rtol=2e-6):
-    """Same expert set per token (the order of an unsorted top-k is not part of the
-    contract) and the same weight for each (token, expert) within fp32 rounding."""
-    ids = np.asarray(ids)
-    ref_ids = np.asarray(ref_ids)
-    o, r = np.argsort(ids, 1), np.argsort(ref_ids, 1)
-    np.testing.assert_array_equal(np.take_along_axis(ids, o, 1), np.take_along_axis(ref_ids, r, 1))
-    np.testing.assert_allclose(np.take_along_axis(np.asarray(wts), o, 1),
-                               np.take_along_axis(np.asarray(ref_wts), r, 1), rtol=rtol, atol=1e-9)
+    """The reference's routing slot for slot: the same expert ids in the same order
+    (torch.topk(sorted=False)'s order on CPU) and the same weight in each slot within
+    fp32 rounding (the renormalising sum runs in slot order on both sides)."""
+    np.testing.assert_array_equal(np.asarray(ids), np.asarray(ref_ids))
+    np.testing.assert_allclose(np.asarray(wts), np.asarray(ref_wts), rtol=rtol, atol=1e-9)
+
+
+def stable_plan(ref_ids, lo, hi):
+    """Counts, offsets and permutation of experts [lo, hi) from the reference's ids:
+    the stable argsort of the flat ids restricted to the shard."""
+    flat = np.asarray(ref_ids).ravel()
+    order = np.argsort(flat, kind="stable")
+    perm = np.array([q for q in order if lo <= flat[q] < hi], dtype=np.int64)
+    counts = np.bincount(flat[(flat >= lo) & (flat < hi)] - lo, minlength=hi - lo)
+    return counts, np.concatenate([[0], np.cumsum(counts)]), perm

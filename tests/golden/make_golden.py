@@ -3,7 +3,10 @@
 Run in a container that has the reference's Python dependencies (transformers
 5.5.0 is what this repository was checked against):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [--only name,name]
+
+Every shape is a multiple of 64 in hidden and inter: the tcgen05 kernels (the
+only expert path) take K-tiles of 64.
 
 GPT-OSS fixtures come from HuggingFace transformers' own CPU modules -- the code
 the reference loads for GPT-OSS (phase0/pipeline.py:126-182):
@@ -82,16 +85,18 @@ CASES = [
     # name, shape, tokens, seed, options
     ("gptoss_cfg0_seed0", synth.GPT_OSS_20B, 5, 0, {}),
     ("gptoss_small_seed0", dict(num_experts=8, top_k=4, hidden=256, inter=128), 7, 0, {}),
-    ("gptoss_small_seed1", dict(num_experts=16, top_k=4, hidden=128, inter=96), 33, 1, {}),
+    ("gptoss_small_seed1", dict(num_experts=16, top_k=4, hidden=128, inter=128), 33, 1, {}),
     ("gptoss_small_m1", dict(num_experts=8, top_k=2, hidden=64, inter=64), 1, 2, {}),
     ("gptoss_small_ties", dict(num_experts=32, top_k=4, hidden=64, inter=64), 64, 3, {"ties": True}),
-    ("gptoss_small_e128", dict(num_experts=128, top_k=4, hidden=96, inter=64), 16, 4, {"ties": True}),
+    ("gptoss_small_e128", dict(num_experts=128, top_k=4, hidden=128, inter=64), 16, 4, {"ties": True}),
 ]
 
 
-def main():
+def main(only=None):
     os.makedirs(HERE, exist_ok=True)
     for name, shape, M, seed, opt in CASES:
+        if only and name not in only:
+            continue
         layer = synth.make_gpt_oss_layer(**shape, seed=seed)
         if opt.get("ties"):
             layer = tie_heavy_router(layer, seed)
@@ -113,4 +118,8 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default=None, help="comma-separated case names")
+    a = ap.parse_args()
+    main(a.only.split(",") if a.only else None)

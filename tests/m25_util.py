@@ -18,7 +18,7 @@ def load_case(path):
     seed = int(f["seed"])
     layer = synth.make_m25_layer(**shape, seed=seed, global_scale=float(f["global_scale"]))
     x = synth.make_tokens(int(f["M"]), layer.hidden, seed=seed)
-    return dict(fixture=f, shape=shape, layer=layer, x=x, seed=seed)
+    return dict(fixture=f, shape=shape, layer=layer, x=x, seed=seed, path=path)
 
 
 def dequant_expert(layer, e, device=None, bf16=False):
@@ -63,6 +63,24 @@ def exact_in_bf16(case):
 
 def fixture_y(case):
     return bf16_bits_to_f32(case["fixture"]["y"])
+
+
+def is_f32_fixture(case):
+    """The fixture holds HF's MiniMaxM2Experts.forward run in fp32 on the exact NVFP4
+    weights ("y_f32"), not the bf16 module's output."""
+    return "y_f32" in case["fixture"]
+
+
+def bf16_module_distance(case):
+    """rel-L2 of HF's bf16 module (the fixture of the same layer and tokens held in
+    bf16) from the fp32 exact-weight evaluation of an _f32 fixture: the reference
+    CPU arithmetic's own distance to the exact-weight layer."""
+    import os
+    from tests.dsv3_util import metrics
+    path = case["path"].replace("_f32.npz", ".npz")
+    bf = np.load(path)
+    assert int(bf["seed"]) == case["seed"] and str(bf["digest"]) == str(case["fixture"]["digest"])
+    return metrics(bf16_bits_to_f32(bf["y"]), case["fixture"]["y_f32"])["rel_l2"]
 
 
 def metrics_of(got, ref):

@@ -46,6 +46,10 @@ def test_desc_validation():
     assert lib.flyai_moe_check_desc(ctypes.byref(good_desc(format=7))) == _lib.ERR_UNSUPPORTED
     assert lib.flyai_moe_check_desc(ctypes.byref(good_desc(top_k=9))) == _lib.ERR_INVALID_ARG
     assert lib.flyai_moe_check_desc(ctypes.byref(good_desc(hidden=2880 + 16))) == _lib.ERR_ALIGNMENT
+    # one expert path (tcgen05): K-tiles of 64, at most 3072 per projection
+    assert lib.flyai_moe_check_desc(ctypes.byref(good_desc(hidden=96))) == _lib.ERR_ALIGNMENT
+    assert lib.flyai_moe_check_desc(ctypes.byref(good_desc(inter=2880 + 32))) == _lib.ERR_ALIGNMENT
+    assert lib.flyai_moe_check_desc(ctypes.byref(good_desc(hidden=3136))) == _lib.ERR_UNSUPPORTED
     assert lib.flyai_moe_check_desc(ctypes.byref(good_desc(expert_end=129))) == _lib.ERR_INVALID_ARG
     d = good_desc()
     d.reserved[3] = 1

@@ -31,6 +31,19 @@ def _mailboxes(shard, n):
     return boxes
 
 
+class _RawInt32:
+    """A device buffer the library allocated, seen by torch without a copy."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = dict(shape=(n,), typestr="<i4", data=(ptr, False),
+                                             version=3)
+
+
+def _flag_words(box, n=64):
+    """The first n int32 words of a mailbox (flags, then failure words) as a tensor."""
+    return torch.as_tensor(_RawInt32(box.value, n), device="cuda")
+
+
 def _peers(boxes, rank, epoch):
     p = _lib.EpPeers()
     p.world, p.rank, p.epoch, p.reserved = len(boxes), rank, epoch, 0
@@ -87,6 +100,46 @@ def test_two_shards_in_one_process_reproduce_the_layer(layer):
             torch.cuda.synchronize()
             assert shards[0].read_error()[0] == 0
             assert torch.equal(y, y_full), epoch
+    finally:
+        torch.cuda.synchronize()
+        for b in boxes:
+            _lib.call("flyai_moe_ep_free", b)
+
+
+def test_combine_reports_a_rank_whose_expert_kernel_gave_up(layer):
+    """A rank whose expert kernel gave up on a bounded wait raises its failure word
+    to the epoch before its flag.  Here rank 1's flag and failure word are written
+    from the host (the expert kernel's path to them needs a wait that runs out);
+    rank 0's combine then folds nothing, reports the timeout bit and returns zeros
+    instead of a layer missing rank 1's rows."""
+    E = layer.router_w.shape[0]
+    x = synth.make_tokens(5, layer.router_w.shape[1], seed=10).cuda()
+    rank0 = Mxfp4MoE.from_layer(layer, expert_range=(0, E // 2), max_tokens=8, device="cuda")
+    boxes = _mailboxes(rank0, 2)
+    try:
+        epoch = 1
+        peers = _peers(boxes, 0, epoch)
+        words = _flag_words(boxes[0])
+        words[1] = epoch           # rank 1's flag in rank 0's mailbox
+        words[16 + 1] = epoch      # and its failure word (kEpFailWord + rank)
+        rank0.route(x, logits=False)
+        assert rank0.experts_ep(x, peers) == _lib.OK
+        y = rank0.combine_ep(5, peers)
+        torch.cuda.synchronize()
+        bits, _ = rank0.read_error()
+        assert bits & K_ERR_WAIT_TIMEOUT
+        assert torch.count_nonzero(y) == 0
+        # a later epoch without a failure word folds normally again
+        shard1 = Mxfp4MoE.from_layer(layer, expert_range=(E // 2, E), max_tokens=8, device="cuda")
+        full = Mxfp4MoE.from_layer(layer, max_tokens=8, device="cuda")
+        y_full, _, _ = full.forward(x)
+        for r, sh in ((1, shard1), (0, rank0)):
+            sh.route(x, logits=False)
+            assert sh.experts_ep(x, _peers(boxes, r, 2)) == _lib.OK
+        y2 = rank0.combine_ep(5, _peers(boxes, 0, 2))
+        torch.cuda.synchronize()
+        assert rank0.read_error()[0] == 0
+        assert torch.equal(y2, y_full)
     finally:
         torch.cuda.synchronize()
         for b in boxes:

@@ -72,3 +72,46 @@ def test_noalloc_refuses_descriptor_beyond_its_array():
     torch.cuda.synchronize()
     assert torch.equal(ids1, ids0)
     np.testing.assert_array_equal(bf16_tensor_to_f32(y1), bf16_tensor_to_f32(y0))
+
+
+def _noalloc_fp(moe, x):
+    """The no-allocation call for an FP8 or NVFP4 layer (fp32 routing weights)."""
+    M = x.shape[0]
+    y = torch.empty(M, moe.hidden, dtype=torch.bfloat16, device=x.device)
+    ids = torch.empty(M, moe.top_k, dtype=torch.int32, device=x.device)
+    wts = torch.empty(M, moe.top_k, dtype=torch.float32, device=x.device)
+    st = _lib.load().flyai_moe_forward_noalloc(
+        ctypes.byref(moe.desc), M, ctypes.c_void_p(x.data_ptr()), ctypes.byref(moe.weights),
+        ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(ids.data_ptr()),
+        ctypes.c_void_p(wts.data_ptr()), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == _lib.OK, _lib.load().flyai_moe_strerror(st).decode()
+    return y, ids, wts
+
+
+def test_noalloc_array_shared_across_weight_formats():
+    """One array serves every descriptor: calls alternate between an MXFP4, an NVFP4
+    and an FP8 layer (whose intermediate data sit at different offsets of the array)
+    and each result equals the workspace entry point's for the same layer."""
+    from flyai_b200.dsv3 import Fp8MoE
+    from flyai_b200.m25 import Nvfp4MoE
+    mx = Mxfp4MoE.from_layer(synth.make_gpt_oss_layer(num_experts=32, top_k=4, hidden=256,
+                                                      inter=192, seed=3), max_tokens=16, device="cuda")
+    nv = Nvfp4MoE.from_layer(synth.make_m25_layer(num_experts=64, top_k=8, hidden=256, inter=256,
+                                                  seed=4), max_tokens=16, device="cuda")
+    f8 = Fp8MoE.from_layer(synth.make_dsv3_layer(num_experts=32, top_k=4, hidden=256, inter=128,
+                                                 n_group=4, topk_group=2, seed=5),
+                           max_tokens=16, device="cuda")
+    for rnd in range(2):
+        for name, moe in (("mxfp4", mx), ("nvfp4", nv), ("fp8", f8)):
+            x = synth.make_tokens(5 + 4 * rnd, 256, seed=50 + rnd, device="cuda")
+            if name == "mxfp4":
+                y_ref, ids_ref, _ = moe.forward(x)
+                y, ids, _ = _noalloc(moe, x)
+            else:
+                ids_ref = torch.empty(x.shape[0], moe.top_k, dtype=torch.int32, device="cuda")
+                wts_ref = torch.empty(x.shape[0], moe.top_k, dtype=torch.float32, device="cuda")
+                y_ref = moe.forward(x, ids=ids_ref, wts=wts_ref)
+                y, ids, _ = _noalloc_fp(moe, x)
+            torch.cuda.synchronize()
+            assert torch.equal(ids, ids_ref), (name, rnd)
+            assert torch.equal(y, y_ref), (name, rnd)
