@@ -86,21 +86,30 @@ REL_L2_TOL = 5e-3
 MAX_ABS_TOL = 2e-2
 
 
-def assert_within_tolerance(y, y_ref, ulp_frac1=0.999, ulp_max=2):
-    """The layer tolerance plus an element-wise bound in bf16 steps (bf16_steps):
-    at least ulp_frac1 of the elements within one step of the reference and none
-    further than ulp_max (None skips that check).  The GPT-OSS layer rounds to bf16
-    after every op exactly where the reference does; only fp32 summation order
-    differs, which moves an output by at most a step or two.  The metrics
-    returned carry the unscaled max-abs and the step statistics either way."""
+def bf16_peak_ulp(y_ref):
+    """One bf16 ulp at the largest |y_ref| (the spacing of bf16 values there)."""
+    peak = float(np.abs(np.asarray(y_ref, np.float64)).max()) if np.size(y_ref) else 0.0
+    return float(np.exp2(np.floor(np.log2(peak)) - 7)) if peak > 0 else 0.0
+
+
+def assert_within_tolerance(y, y_ref, ulp_frac1=0.999, peak_ulps=1.0):
+    """The layer tolerance plus element-wise bounds in bf16 steps: at least
+    ulp_frac1 of the elements within one step of the reference (bf16_steps), and
+    every element within peak_ulps bf16 ulps at the output's peak, i.e. an
+    absolute error no larger than one rounding of the largest outputs.  (A step
+    bound on every element cannot hold: the reference folds the experts' rows with
+    a bf16 rounding after every add, so an output that cancels to a small value
+    carries the rounding of partial sums near the peak.)  The metrics returned
+    carry the unscaled max-abs and the step statistics either way."""
     m = parity_metrics(y, y_ref)
     m.update(ulp_stats(y, y_ref))
+    m["peak_ulp"] = bf16_peak_ulp(y_ref)
     assert m["rel_l2"] <= REL_L2_TOL, m
     assert m["max_abs"] <= MAX_ABS_TOL * max(m["max_ref"], 1.0), m
     if ulp_frac1 is not None:
         assert m["ulp_le1"] >= ulp_frac1, m
-    if ulp_max is not None:
-        assert m["ulp_max"] <= ulp_max, m
+    if peak_ulps is not None:
+        assert m["max_abs"] <= peak_ulps * m["peak_ulp"], m
     return m
 
 
