@@ -21,9 +21,11 @@ ERR_ABI = -6
 FMT_MXFP4 = 1
 FMT_FP8_BLOCK = 2
 FMT_NVFP4 = 3
+FMT_FP4_W4A8 = 4
 GATE_SOFTMAX_TOPK = 1
 GATE_SIGMOID_GROUP = 2
 GATE_SIGMOID_BF16 = 3
+GATE_SQRTSOFTPLUS = 4
 ACT_GPTOSS_SWIGLU = 1
 ACT_SILU = 2
 ACT_SILU_BF16 = 3
@@ -39,7 +41,8 @@ EXPORTS = (
     "flyai_moe_ep_free", "flyai_moe_ipc_get_handle", "flyai_moe_ipc_open", "flyai_moe_ipc_close",
     "flyai_moe_experts_ep", "flyai_moe_combine_ep",
     "flyai_moe_forward_noalloc", "flyai_moe_read_error", "flyai_moe_pack_fp8",
-    "flyai_moe_pack_nvfp4",
+    "flyai_moe_pack_nvfp4", "flyai_moe_pack_fp4", "flyai_moe_pack_shared_fp8",
+    "flyai_moe_route_hash",
 )
 
 
@@ -99,6 +102,9 @@ def load():
         "flyai_moe_pack_mxfp4": ([pd, i32, vp, vp, vp, vp], ctypes.c_int),
         "flyai_moe_pack_fp8": ([pd, i32, vp, vp, vp, vp], ctypes.c_int),
         "flyai_moe_pack_nvfp4": ([pd, i32, vp, vp, vp, vp, vp], ctypes.c_int),
+        "flyai_moe_pack_fp4": ([pd, i32, vp, vp, vp, vp], ctypes.c_int),
+        "flyai_moe_pack_shared_fp8": ([pd, i32, vp, vp, vp, vp], ctypes.c_int),
+        "flyai_moe_route_hash": ([pd, i32, vp, vp, vp, i32, pw, vp, vp, vp, vp, sz, vp], ctypes.c_int),
         "flyai_moe_workspace_bytes": ([pd, ctypes.POINTER(sz)], ctypes.c_int),
         "flyai_moe_route": ([pd, i32, vp, pw, vp, vp, vp, vp, sz, vp], ctypes.c_int),
         "flyai_moe_experts": ([pd, i32, vp, pw, vp, vp, sz, vp], ctypes.c_int),

@@ -20,7 +20,8 @@ static bool aligned(const void* p, size_t a) {
 // The FP8 and NVFP4 layers share the routing plan, workspace and combine
 // (fp8_moe.cu); their expert kernels differ.
 static bool is_fp8(const flyai_moe_desc& d) {
-  return d.format == FLYAI_FMT_FP8_BLOCK || d.format == FLYAI_FMT_NVFP4;
+  return d.format == FLYAI_FMT_FP8_BLOCK || d.format == FLYAI_FMT_NVFP4 ||
+         d.format == FLYAI_FMT_FP4_W4A8;
 }
 
 static int check_desc(const flyai_moe_desc* d) {
@@ -56,6 +57,17 @@ static int check_desc(const flyai_moe_desc* d) {
         d->topk_group > d->n_group)
       return FLYAI_ERR_INVALID_ARG;
     if (d->top_k > d->topk_group * (d->num_experts / d->n_group)) return FLYAI_ERR_INVALID_ARG;
+    if (!(d->route_scale > 0.f) || d->n_shared < 0 || d->n_shared > 1) return FLYAI_ERR_INVALID_ARG;
+    if (!(d->swiglu_limit >= 0.f) || d->swiglu_alpha != 0.f) return FLYAI_ERR_INVALID_ARG;
+    if (d->max_tokens > kF8MaxTokens) return FLYAI_ERR_UNSUPPORTED;
+    return FLYAI_OK;
+  }
+  if (d->format == FLYAI_FMT_FP4_W4A8) {
+    if (d->gating != FLYAI_GATE_SQRTSOFTPLUS) return FLYAI_ERR_UNSUPPORTED;
+    if (d->activation != FLYAI_ACT_SILU) return FLYAI_ERR_UNSUPPORTED;
+    if (d->hidden % 128 || d->inter % 128) return FLYAI_ERR_ALIGNMENT;
+    if (d->num_experts % 32 || d->num_experts > kF8MaxExperts) return FLYAI_ERR_UNSUPPORTED;
+    if (d->n_group != 1 || d->topk_group != 1) return FLYAI_ERR_INVALID_ARG;
     if (!(d->route_scale > 0.f) || d->n_shared < 0 || d->n_shared > 1) return FLYAI_ERR_INVALID_ARG;
     if (!(d->swiglu_limit >= 0.f) || d->swiglu_alpha != 0.f) return FLYAI_ERR_INVALID_ARG;
     if (d->max_tokens > kF8MaxTokens) return FLYAI_ERR_UNSUPPORTED;
@@ -126,6 +138,8 @@ static int launch_layer_experts(const flyai_moe_desc& d, int M, const void* x,
       return launch_nvp_experts(d, M, w, y, rows, fw, s, g_prof_start.load(), g_prof_stop.load());
     return launch_nv4_experts(d, M, x, w, y, rows, fw, s, g_prof_start.load(), g_prof_stop.load());
   }
+  if (d.format == FLYAI_FMT_FP4_W4A8)
+    return launch_v4_experts(d, M, w, y, rows, fw, s, g_prof_start.load(), g_prof_stop.load());
   return launch_fp8_experts(d, M, x, w, y, rows, fw, s, g_prof_start.load(), g_prof_stop.load());
 }
 
@@ -190,7 +204,8 @@ int flyai_moe_set_profile_events(void* start, void* stop) {
 int flyai_moe_packed_bytes(const flyai_moe_desc* desc, int32_t proj, size_t* bytes) {
   FLYAI_TRY(check_desc(desc));
   if (!bytes || (proj != FLYAI_PROJ_W13 && proj != FLYAI_PROJ_W2)) return FLYAI_ERR_INVALID_ARG;
-  *bytes = desc->format == FLYAI_FMT_NVFP4 ? nv4_packed_bytes(*desc, proj)
+  *bytes = desc->format == FLYAI_FMT_NVFP4     ? nv4_packed_bytes(*desc, proj)
+           : desc->format == FLYAI_FMT_FP4_W4A8 ? v4_packed_bytes(*desc, proj)
            : is_fp8(*desc)                 ? fp8_packed_bytes(*desc, proj)
                                            : tc_packed_bytes(*desc, proj);
   return FLYAI_OK;
@@ -216,6 +231,28 @@ int flyai_moe_pack_fp8(const flyai_moe_desc* desc, int32_t proj, const void* wei
   if (!weight || !scale || !packed) return FLYAI_ERR_INVALID_ARG;
   if (!aligned(weight, 16) || !aligned(packed, 16) || !aligned(scale, 4)) return FLYAI_ERR_ALIGNMENT;
   return launch_fp8_pack(*desc, proj, weight, scale, packed, static_cast<cudaStream_t>(stream));
+}
+
+int flyai_moe_pack_fp4(const flyai_moe_desc* desc, int32_t proj, const void* blocks,
+                       const void* scales, void* packed, void* stream) {
+  FLYAI_TRY(check_desc(desc));
+  if (proj != FLYAI_PROJ_W13 && proj != FLYAI_PROJ_W2) return FLYAI_ERR_INVALID_ARG;
+  if (desc->format != FLYAI_FMT_FP4_W4A8) return FLYAI_ERR_UNSUPPORTED;
+  if (desc->expert_end == desc->expert_begin) return FLYAI_OK;
+  if (!blocks || !scales || !packed) return FLYAI_ERR_INVALID_ARG;
+  if (!aligned(blocks, 16) || !aligned(packed, 16) || !aligned(scales, 4)) return FLYAI_ERR_ALIGNMENT;
+  return launch_v4_pack_fp4(*desc, proj, blocks, scales, packed, static_cast<cudaStream_t>(stream));
+}
+
+int flyai_moe_pack_shared_fp8(const flyai_moe_desc* desc, int32_t proj, const void* weight,
+                              const void* scale, void* packed, void* stream) {
+  FLYAI_TRY(check_desc(desc));
+  if (proj != FLYAI_PROJ_W13 && proj != FLYAI_PROJ_W2) return FLYAI_ERR_INVALID_ARG;
+  if (desc->format != FLYAI_FMT_FP4_W4A8) return FLYAI_ERR_UNSUPPORTED;
+  if (desc->n_shared == 0) return FLYAI_OK;
+  if (!weight || !scale || !packed) return FLYAI_ERR_INVALID_ARG;
+  if (!aligned(weight, 16) || !aligned(packed, 16)) return FLYAI_ERR_ALIGNMENT;
+  return launch_v4_pack_shared(*desc, proj, weight, scale, packed, static_cast<cudaStream_t>(stream));
 }
 
 int flyai_moe_pack_nvfp4(const flyai_moe_desc* desc, int32_t proj, const void* blocks,
@@ -256,6 +293,26 @@ int flyai_moe_route(const flyai_moe_desc* desc, int32_t M, const void* x,
   const Workspace ws = carve_workspace(*desc, desc->max_tokens, workspace);
   return launch_route(*desc, M, x, *w, logits, topk_ids, topk_weights, ws,
                       static_cast<cudaStream_t>(stream));
+}
+
+int flyai_moe_route_hash(const flyai_moe_desc* desc, int32_t M, const void* x, const int32_t* input_ids,
+                         const int32_t* tid2eid, int32_t vocab, const flyai_moe_weights* w, void* logits,
+                         int32_t* topk_ids, void* topk_weights, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  FLYAI_TRY(check_desc(desc));
+  FLYAI_TRY(check_tokens(desc, M));
+  FLYAI_TRY(check_workspace(desc, workspace, workspace_bytes));
+  FLYAI_TRY(check_weights(desc, w, true, false));
+  if (desc->gating != FLYAI_GATE_SQRTSOFTPLUS) return FLYAI_ERR_UNSUPPORTED;
+  if (M > 0 && (!x || !input_ids || !tid2eid)) return FLYAI_ERR_INVALID_ARG;
+  if (vocab < 1) return FLYAI_ERR_INVALID_ARG;
+  if (x && !aligned(x, 16)) return FLYAI_ERR_ALIGNMENT;
+  if ((input_ids && !aligned(input_ids, 4)) || (tid2eid && !aligned(tid2eid, 4))) return FLYAI_ERR_ALIGNMENT;
+  if (!w->router_b || !aligned(w->router_b, 4)) return FLYAI_ERR_INVALID_ARG;
+  const Fp8Workspace fw = carve_fp8_workspace(*desc, desc->max_tokens, workspace);
+  return launch_fp8_route(*desc, M, x, *w, static_cast<float*>(logits), topk_ids,
+                          static_cast<float*>(topk_weights), fw, static_cast<cudaStream_t>(stream),
+                          tid2eid, input_ids, vocab);
 }
 
 int flyai_moe_read_plan(const flyai_moe_desc* desc, int32_t M, const void* workspace,

@@ -31,6 +31,7 @@
 #include "tc_bank.cuh"
 #include "tcgen05.cuh"
 #include "torch_topk.cuh"
+#include "v4.cuh"
 
 namespace flyai {
 
@@ -160,7 +161,59 @@ struct F8RouteParams {
   int4* chunk_info;
   int32_t* chunk_done;
   int32_t* ticket;       // [0] token groups finished, [1 + g] CTAs of group g finished
+  // DeepSeek-V4 gate (FLYAI_GATE_SQRTSOFTPLUS): scores sqrt(softplus(logit)),
+  // torch.topk sorted (descending, torch's order among ties), and on a
+  // hash-routed layer ids = tid2eid[input_ids[t]] instead of the top-k
+  int score_fn;          // 0: sigmoid, 1: sqrt(softplus)
+  int sorted;            // top-k order: torch.topk(sorted=True) instead of sorted=False
+  const int32_t* tid2eid;    // [vocab, k] or null
+  const int32_t* input_ids;  // [M] (with tid2eid)
+  int vocab;
+  int ue8m0;             // act_quant scales 2^ceil(log2(amax/448)) (scale_fmt "ue8m0")
+  int32_t* err;          // error word (bit 2: an input id or table entry out of range)
 };
+
+constexpr int32_t kErrBadIndex = 2;
+
+// The gate's score of a logit: sigmoid (DeepSeek-V3, MiniMax-M2) or
+// sqrt(softplus) with torch's threshold 20 (DeepSeek-V4, model.py:575-576).
+__device__ __forceinline__ float f8_score(int fn, float l) {
+  if (fn == 1) return sqrtf(l > 20.f ? l : log1pf(expf(l)));
+  return __frcp_rn(__fadd_rn(1.f, expf(-l)));
+}
+
+// The ids of token t when the layer is hash-routed: tid2eid[input_ids[t]], an id
+// or table entry out of range recorded in the error word (and replaced by 0).
+__device__ __forceinline__ int f8_hash_id(const F8RouteParams& p, int t, int r) {
+  int tok = __ldg(&p.input_ids[t]);
+  if (tok < 0 || tok >= p.vocab) {
+    atomicOr(p.err, kErrBadIndex);
+    tok = 0;
+  }
+  int id = __ldg(&p.tid2eid[static_cast<size_t>(tok) * p.k + r]);
+  if (id < 0 || id >= p.E) {
+    atomicOr(p.err, kErrBadIndex);
+    id = 0;
+  }
+  return id;
+}
+
+// The top-k of the choice row (already in row[0..E)): torch.topk's order, sorted
+// or not, or the hash table's ids.  Leaves the ids in row[0..k).i.
+__device__ __forceinline__ void f8_topk_row(const F8RouteParams& p, int t, KV* row, void* tks) {
+  const int lane = threadIdx.x & 31;
+  if (p.tid2eid) {
+    __syncwarp();
+    if (lane < p.k) row[lane].i = f8_hash_id(p, t, lane);
+    __syncwarp();
+    return;
+  }
+  torch_topk_warp(row, p.E, p.k, tks);
+  if (p.sorted && p.k * 64 > p.E) {   // std::sort(q, q+k-1) after nth_element
+    if (lane == 0) kv_insertion_sort(row, 0, p.k - 1);
+    __syncwarp();
+  }
+}
 
 // Exclusive prefix of one int per thread over the block; *total = block sum.
 __device__ int f8_block_scan(int v, int* tmp, int* total) {
@@ -192,13 +245,15 @@ __device__ int f8_block_scan(int v, int* tmp, int* total) {
 }
 
 // act_quant of one 128-element block of a bf16 row by one warp (4 elements per lane).
-__device__ __forceinline__ void f8_quant_block(const uint16_t* src, uint8_t* q, float* sc, int lane) {
+// ue8m0: the scale is 2^ceil(log2(amax/448)) (scale_fmt "ue8m0"), else amax/448.
+__device__ __forceinline__ void f8_quant_block(const uint16_t* src, uint8_t* q, float* sc, int lane,
+                                               int ue8m0) {
   const uint2 raw = __ldg(reinterpret_cast<const uint2*>(src + lane * 4));
   const float v[4] = {__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xFFFF0000u),
                       __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xFFFF0000u)};
   float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
   a = fmaxf(warp_max(a), 1e-4f);
-  const float s = __fmul_rn(a, kF8Inv448);
+  const float s = ue8m0 ? exp2_int(ue8m0_exp(a, kF8Inv448)) : __fmul_rn(a, kF8Inv448);
   uint32_t packed = 0;
 #pragma unroll
   for (int j = 0; j < 4; ++j) packed |= f32_to_e4m3(__fdiv_rn(v[j], s)) << (8 * j);
@@ -243,7 +298,7 @@ __device__ void f8_select_token(const F8RouteParams& p, int t, KV* row, void* tk
     if (j < nj) {
       const int e = lane * nj + j;
       const float l = __ldcg(p.logits + static_cast<size_t>(t) * E + e);
-      const float s = __frcp_rn(__fadd_rn(1.f, expf(-l)));
+      const float s = f8_score(p.score_fn, l);
       sc[j] = s;
       ch[j] = __fadd_rn(s, __ldg(p.bias + e));
       row[e].v = ch[j];
@@ -276,7 +331,7 @@ __device__ void f8_select_token(const F8RouteParams& p, int t, KV* row, void* tk
 #pragma unroll
   for (int j = 0; j < 16; ++j)
     if (j < nj) row[lane * nj + j] = KV{ch[j], lane * nj + j};
-  torch_topk_warp(row, E, k, tks);
+  f8_topk_row(p, t, row, tks);
   int my_id = 0;
   float my_w = 0.f;
   for (int r = 0; r < k; ++r) {
@@ -324,7 +379,7 @@ __device__ void f8_select_token_256(const F8RouteParams& p, int t, KV* row, void
   float sc[8], ch[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    sc[j] = __frcp_rn(__fadd_rn(1.f, expf(-lv[j])));
+    sc[j] = f8_score(p.score_fn, lv[j]);
     ch[j] = __fadd_rn(sc[j], bv[j]);
   }
   if (p.n_group > 1 && p.n_group > p.topk_group) {
@@ -382,7 +437,7 @@ __device__ void f8_select_token_256(const F8RouteParams& p, int t, KV* row, void
   __syncwarp();
 #pragma unroll
   for (int j = 0; j < 8; ++j) row[lane * 8 + j] = KV{ch[j], lane * 8 + j};
-  torch_topk_warp(row, 256, k, tks);
+  f8_topk_row(p, t, row, tks);
   int my_id = 0;
   float my_w = 0.f;
   for (int r = 0; r < k; ++r) {
@@ -530,7 +585,7 @@ __global__ void __launch_bounds__(kF8RouteThreads, kNv ? 1 : 2) f8_route_kernel(
       const int t = u / KB, kb = u - t * KB;
       f8_quant_block(p.x + static_cast<size_t>(t) * H + kb * kF8Blk,
                      p.xq + static_cast<size_t>(t) * H + kb * kF8Blk,
-                     p.xs + static_cast<size_t>(t) * KB + kb, lane);
+                     p.xs + static_cast<size_t>(t) * KB + kb, lane, p.ue8m0);
     }
   }
   __syncthreads();
@@ -659,9 +714,17 @@ __global__ void __launch_bounds__(kF8RouteThreads, kNv ? 1 : 2) f8_route_kernel(
 
 int launch_fp8_route(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_weights& w,
                      float* logits, int32_t* topk_ids, float* topk_weights,
-                     const Fp8Workspace& ws, cudaStream_t stream) {
+                     const Fp8Workspace& ws, cudaStream_t stream, const int32_t* tid2eid,
+                     const int32_t* input_ids, int vocab) {
   if (M == 0) return FLYAI_OK;
   F8RouteParams prm{};
+  prm.score_fn = d.gating == FLYAI_GATE_SQRTSOFTPLUS ? 1 : 0;
+  prm.sorted = d.gating == FLYAI_GATE_SQRTSOFTPLUS ? 1 : 0;
+  prm.ue8m0 = is_v4(d) ? 1 : 0;
+  prm.tid2eid = tid2eid;
+  prm.input_ids = input_ids;
+  prm.vocab = vocab;
+  prm.err = ws.err;
   prm.x = static_cast<const uint16_t*>(x);
   prm.w = static_cast<const uint16_t*>(w.router_w);
   prm.bias = static_cast<const float*>(w.router_b);
@@ -1101,9 +1164,18 @@ __global__ void __launch_bounds__(128) f8_combine_kernel(const __grid_constant__
   int id[kMaxTopK];
 #pragma unroll
   for (int j = 0; j < kMaxTopK; ++j) id[j] = j < p.k ? __ldg(&p.ids[t * p.k + j]) : 0x7fffffff;
+  // an expert named by several slots (a hash-routed layer) counts once, with its
+  // last slot: the reference's y[idx] += v writes every duplicate back and the
+  // last write wins (vendor/deepseek_v4_ref/inference/model.py:641-644)
+  uint32_t used = 0;
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j)
+#pragma unroll
+    for (int j2 = j + 1; j2 < kMaxTopK; ++j2)
+      if (j2 < p.k && id[j2] == id[j]) used |= 1u << j;
+  const int live = p.k - __popc(used);
   // flat pair rows in ascending expert id, then every row's load in flight at once
   int order[kMaxTopK];
-  uint32_t used = 0;
 #pragma unroll
   for (int r = 0; r < kMaxTopK; ++r) {
     int best = 0, bid = 0x7fffffff;
@@ -1114,7 +1186,7 @@ __global__ void __launch_bounds__(128) f8_combine_kernel(const __grid_constant__
         best = j;
       }
     used |= 1u << best;
-    order[r] = r < p.k ? t * p.k + best : -1;
+    order[r] = r < live ? t * p.k + best : -1;
   }
   uint4 v[kMaxTopK + 1];
 #pragma unroll

@@ -88,8 +88,11 @@ struct Fp8Workspace {
 
 __host__ __device__ inline bool is_nv4(const flyai_moe_desc& d) { return d.format == FLYAI_FMT_NVFP4; }
 __host__ __device__ inline int layer_chunk(const flyai_moe_desc& d) { return is_nv4(d) ? kNvChunk : kF8Chunk; }
-// bytes of the B block of one chunk and one 128-wide K block
-__host__ __device__ inline int layer_bblock(const flyai_moe_desc& d) { return is_nv4(d) ? kNvBBytes : kF8BBytes; }
+// bytes of the B block of one chunk and one 128-wide K block (FLYAI_FMT_FP4_W4A8:
+// 16 token rows of e4m3 and their 512-byte scale chunk)
+__host__ __device__ inline int layer_bblock(const flyai_moe_desc& d) {
+  return is_nv4(d) ? kNvBBytes : d.format == FLYAI_FMT_FP4_W4A8 ? kF8BTile + 512 : kF8BBytes;
+}
 
 // Chunks a batch of M tokens can need: every non-empty expert rounds its
 // count up to a chunk once, plus the shared expert's chunks.
@@ -161,9 +164,11 @@ int launch_fp8_pack(const flyai_moe_desc& d, int proj, const void* weight, const
 // Gate (grouped sigmoid, or the bf16-logit sigmoid gate of FLYAI_GATE_SIGMOID_BF16)
 // + token rows quantised (FP8) or split into terms (NVFP4) + routing plan;
 // logits/ids/weights outputs may be null.
+// tid2eid / input_ids / vocab: a hash-routed layer (FLYAI_GATE_SQRTSOFTPLUS).
 int launch_fp8_route(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_weights& w,
                      float* logits, int32_t* topk_ids, float* topk_weights,
-                     const Fp8Workspace& ws, cudaStream_t stream);
+                     const Fp8Workspace& ws, cudaStream_t stream, const int32_t* tid2eid = nullptr,
+                     const int32_t* input_ids = nullptr, int vocab = 0);
 size_t nv4_packed_bytes(const flyai_moe_desc& d, int proj);
 int launch_nv4_pack(const flyai_moe_desc& d, int proj, const void* blocks, const void* scales,
                     const void* global_scale, void* packed, cudaStream_t stream);
@@ -193,6 +198,17 @@ int launch_nvp_route(const flyai_moe_desc& d, int M, const void* x, const flyai_
 int launch_nvp_experts(const flyai_moe_desc& d, int M, const flyai_moe_weights& w, void* y,
                        uint16_t* rows, const Fp8Workspace& ws, cudaStream_t stream,
                        cudaEvent_t ev0, cudaEvent_t ev1);
+// DeepSeek-V4 W4A8 layer (v4_moe.cu): bank sizes and packing (routed experts
+// e2m1 + e8m0/32; the shared expert e4m3 + e8m0 per 128x128), and the expert
+// kernels on the plan the route left in ws (then the fold into y when y is set).
+size_t v4_packed_bytes(const flyai_moe_desc& d, int proj);
+int launch_v4_pack_fp4(const flyai_moe_desc& d, int proj, const void* blocks, const void* scales,
+                       void* packed, cudaStream_t stream);
+int launch_v4_pack_shared(const flyai_moe_desc& d, int proj, const void* weight, const void* scale,
+                          void* packed, cudaStream_t stream);
+int launch_v4_experts(const flyai_moe_desc& d, int M, const flyai_moe_weights& w, void* y,
+                      uint16_t* rows, const Fp8Workspace& ws, cudaStream_t stream, cudaEvent_t ev0,
+                      cudaEvent_t ev1);
 // Rows of the pair-row buffer of a batch of M tokens.
 inline size_t layer_pair_rows(const flyai_moe_desc& d, int M) {
   return static_cast<size_t>(M) * (d.top_k + d.n_shared);

@@ -5,8 +5,8 @@ one), the router and a workspace on one device, and exposes the reference's
 operator surface:
 
 * ``gate(x)``    -> (topk_idx, topk_weight) -- KimiMoEGate.forward
-  (vendor/kimi_k3_ref/modeling_kimi_linear.py:703-759; ids int64, weights fp32,
-  ids in descending choice score rather than torch's unsorted order)
+  (vendor/kimi_k3_ref/modeling_kimi_linear.py:703-759; ids int64 in the order
+  torch.topk(sorted=False) returns them on CPU, weights fp32)
 * ``route(x)``   -> (logits fp32, topk_idx, topk_weight)
 * ``forward(x)`` -> y bf16 -- MoE.forward with fp8 experts and the shared expert
   (vendor/deepseek_v4_ref/inference/model.py:634-649)

@@ -33,6 +33,10 @@ GPT_OSS_120B = dict(num_experts=128, top_k=4, hidden=2880, inter=2880)
 DSV3 = dict(num_experts=256, top_k=8, hidden=7168, inter=2048, n_group=8, topk_group=4,
             route_scale=2.5, n_shared=1)
 M25 = dict(num_experts=256, top_k=8, hidden=3072, inter=1536)
+# DeepSeek-V4-Flash MoE layer (vendor/deepseek_v4_ref/inference/config.json):
+# dim 4096, moe_inter_dim 2048, 256 routed experts (fp4), 6 active, 1 shared
+# expert (fp8), sqrtsoftplus scores, route_scale 1.5, swiglu_limit 10.
+V4 = dict(num_experts=256, top_k=6, hidden=4096, inter=2048, route_scale=1.5, swiglu_limit=10.0)
 
 
 @dataclass
@@ -191,3 +195,69 @@ def make_m25_layer(num_experts, top_k, hidden, inter, seed=0, device="cpu", skew
     bias = bias.bfloat16().float()   # a bf16 checkpoint buffer: same values in fp32 and bf16
     return M25Layer(router_w, bias, inter, top_k, seed, route_scale=route_scale,
                     global_scale=global_scale, device=str(device))
+
+
+@dataclass
+class V4Layer:
+    """Router of a DeepSeek-V4-style W4A8 MoE layer plus seeded expert factories.
+
+    ``expert(e)`` -> (w13 uint8 [2I, H/2] packed e2m1 of [w1; w3] (low nibble =
+    even K), s13 uint8 [2I, H/32] e8m0, w2 uint8 [H, I/2], s2 uint8 [H, I/32]);
+    ``shared()`` -> (w13 e4m3 [2I, H], s13 uint8 [2I/128, H/128] e8m0, w2 e4m3
+    [H, I], s2 uint8 [H/128, I/128] e8m0) -- the shared expert of a "dtype fp8,
+    scale_dtype fp8" checkpoint (power-of-two 128x128 block scales).  ``tid2eid``
+    (int32 [vocab, k], repeats allowed) is set for a hash-routed layer."""
+    router_w: torch.Tensor    # bf16 [E, H]
+    bias: torch.Tensor        # fp32 [E] (score-routed layers)
+    inter: int
+    top_k: int
+    route_scale: float
+    swiglu_limit: float
+    seed: int
+    tid2eid: torch.Tensor = None
+    device: str = "cpu"
+
+    @property
+    def num_experts(self):
+        return self.router_w.shape[0]
+
+    @property
+    def hidden(self):
+        return self.router_w.shape[1]
+
+    def expert(self, e, device=None):
+        device = device or self.device
+        g = torch.Generator(device=device).manual_seed(self.seed * 1_000_003 + 15485863 * (e + 1))
+        rnd = dict(generator=g, device=device)
+        H, I = self.hidden, self.inter
+        w13 = torch.randint(0, 256, (2 * I, H // 2), dtype=torch.uint8, **rnd)
+        s13 = torch.randint(118, 125, (2 * I, H // 32), dtype=torch.uint8, **rnd)
+        w2 = torch.randint(0, 256, (H, I // 2), dtype=torch.uint8, **rnd)
+        s2 = torch.randint(118, 125, (H, I // 32), dtype=torch.uint8, **rnd)
+        return w13, s13, w2, s2
+
+    def shared(self, device=None):
+        device = device or self.device
+        g = torch.Generator(device=device).manual_seed(self.seed * 1_000_003 + 982451653)
+        rnd = dict(generator=g, device=device)
+        H, I, B = self.hidden, self.inter, 128
+        w13 = torch.randn(2 * I, H, **rnd).to(torch.float8_e4m3fn)
+        s13 = torch.randint(117, 121, (2 * I // B, H // B), dtype=torch.uint8, **rnd)
+        w2 = torch.randn(H, I, **rnd).to(torch.float8_e4m3fn)
+        s2 = torch.randint(117, 121, (H // B, I // B), dtype=torch.uint8, **rnd)
+        return w13, s13, w2, s2
+
+
+def make_v4_layer(num_experts, top_k, hidden, inter, route_scale=1.5, swiglu_limit=10.0, seed=0,
+                  device="cpu", hash_vocab=0):
+    """A V4 MoE layer; hash_vocab > 0 makes it hash-routed (the first n_hash_layers
+    of the model) with a random tid2eid table of that many token ids."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    rnd = dict(generator=g, device=device)
+    router_w = (torch.randn(num_experts, hidden, **rnd) * 0.02).bfloat16()
+    bias = torch.randn(num_experts, **rnd) * 0.05
+    tid2eid = None
+    if hash_vocab:
+        tid2eid = torch.randint(0, num_experts, (hash_vocab, top_k), dtype=torch.int32, **rnd)
+    return V4Layer(router_w, bias, inter, top_k, route_scale, swiglu_limit, seed, tid2eid,
+                   str(device))

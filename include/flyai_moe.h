@@ -56,6 +56,11 @@ extern "C" {
 #define FLYAI_FMT_NVFP4          3  /* e2m1 nibbles (low nibble = even K) + e4m3 scale per 16 K + one
                                        fp32 global scale per tensor (ModelOpt NVFP4, the M2.5
                                        checkpoint format loaded at engines/minimax_m25/m25_stage.py:288-311) */
+#define FLYAI_FMT_FP4_W4A8       4  /* DeepSeek-V4 (V4-Flash config: expert_dtype fp4, dtype fp8, scale_fmt
+                                       ue8m0): routed experts e2m1 (low nibble = even K) + one e8m0 scale
+                                       per 32 K; the shared expert e4m3 + one e8m0 scale per 128x128 block;
+                                       activations quantised to e4m3 per 1x128 with power-of-two scales
+                                       (vendor/deepseek_v4_ref/inference/model.py:114-158, 592-649) */
 
 /* gating functions */
 #define FLYAI_GATE_SOFTMAX_TOPK  1  /* GPT-OSS: bf16 logits = xW^T+b, torch.topk, softmax over the k */
@@ -69,6 +74,11 @@ extern "C" {
                                        x route_scale (transformers/models/minimax_m2/modeling_minimax_m2.py
                                        MiniMaxM2TopKRouter; routed_scaling_factor as m25_stage.py:234-235
                                        passes it to FusedMoE); router_b = fp32 [E] bias, weights fp32 */
+#define FLYAI_GATE_SQRTSOFTPLUS  4  /* DeepSeek-V4 Gate.forward (model.py:569-589): fp32 logits of bf16 x
+                                       and W, sqrt(softplus), + bias for the choice only, torch.topk
+                                       (sorted; torch's CPU order among ties) -- or tid2eid[input_ids] on
+                                       a hash-routed layer (flyai_moe_route_hash) --, the unbiased scores
+                                       / their sum x route_scale; router_b = fp32 [E], weights fp32 */
 
 /* expert activations */
 #define FLYAI_ACT_GPTOSS_SWIGLU  1  /* interleaved gate/up, clamp(limit), gate*sigmoid(alpha*gate)*(up+1) */
@@ -94,8 +104,9 @@ typedef struct flyai_moe_desc {
   int32_t expert_begin;   /* experts this process computes: [begin, end)               */
   int32_t expert_end;     /*   (0, E) on one GPU; a contiguous shard under EP          */
   int32_t max_tokens;     /* upper bound on num_tokens the workspace is sized for:     */
-                          /*   <= 64 for FP8_BLOCK, <= 8192 for NVFP4 (calls above 64  */
-                          /*   tokens take its prefill kernels), any for MXFP4          */
+                          /*   <= 64 for FP8_BLOCK and FP4_W4A8, <= 8192 for NVFP4      */
+                          /*   (calls above 64 tokens take its prefill kernels), any    */
+                          /*   for MXFP4                                                */
   float swiglu_limit;     /* GPT-OSS 7.0 (FLYAI_ACT_SILU: 0 = no clamp)                */
   float swiglu_alpha;     /* GPT-OSS 1.702 (FLYAI_ACT_SILU: unused, 0)                 */
   int32_t n_group;        /* FLYAI_GATE_SIGMOID_GROUP: expert groups (1 = ungrouped)   */
@@ -157,6 +168,23 @@ FLYAI_API int flyai_moe_pack_nvfp4(const flyai_moe_desc* desc, int32_t proj, con
                                    const void* scales, const void* global_scale, void* packed,
                                    void* stream);
 
+/* Load-time relayout of DeepSeek-V4 fp4 routed experts into the kernel bank
+ * (FLYAI_FMT_FP4_W4A8).  blocks: uint8 [El, R, K/2] packed e2m1 (the checkpoint's
+ * float4_e2m1fn_x2 weight, low nibble = even K), scales: uint8 [El, R, K/32] e8m0
+ * (its float8_e8m0fnu scale) for the experts of [expert_begin, expert_end);
+ * FLYAI_PROJ_W13 rows are [w1; w3] stacked (R = 2I), FLYAI_PROJ_W2 rows are w2.
+ * Replaces the per-expert fp4 Linear storage of vendor/deepseek_v4_ref/inference/
+ * model.py:133-139 and the bank relayout of engines/deepseek_v4/v4_moe_grouped.py:
+ * 376-550.  packed: flyai_moe_packed_bytes (routed experts, then the shared one). */
+FLYAI_API int flyai_moe_pack_fp4(const flyai_moe_desc* desc, int32_t proj, const void* blocks,
+                                 const void* scales, void* packed, void* stream);
+
+/* The DeepSeek-V4 shared expert into the same bank (after the routed experts):
+ * weight e4m3 [n_shared, R, K], scale uint8 [n_shared, R/128, K/128] e8m0 (an fp8
+ * Linear of a "scale_dtype fp8" checkpoint, model.py:140-145). */
+FLYAI_API int flyai_moe_pack_shared_fp8(const flyai_moe_desc* desc, int32_t proj, const void* weight,
+                                        const void* scale, void* packed, void* stream);
+
 /* Workspace bytes for calls with up to desc->max_tokens tokens.  The layout
  * depends only on the descriptor, so one workspace serves every call with
  * num_tokens <= max_tokens.  Zero-fill a workspace once before its first use:
@@ -173,6 +201,20 @@ FLYAI_API int flyai_moe_route(const flyai_moe_desc* desc, int32_t num_tokens, co
                     const flyai_moe_weights* w, void* logits, int32_t* topk_ids,
                     void* topk_weights, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Router of a hash-routed DeepSeek-V4 layer (layer_id < n_hash_layers): the gate's
+ * scores as flyai_moe_route computes them, but the experts of token t are
+ * tid2eid[input_ids[t]] (int32 [vocab, k] and int32 [M], device memory) instead of
+ * the top-k (model.py:581-582); an expert may repeat within a token, and the fold
+ * then keeps only its last slot, as the reference's y[idx] += does
+ * (engines/deepseek_v4/v4_moe_grouped.py:623-631).  An input id or table entry
+ * out of range sets bit 2 of the error word (flyai_moe_read_error) and reads 0.
+ * FLYAI_GATE_SQRTSOFTPLUS descriptors only; then flyai_moe_experts as usual. */
+FLYAI_API int flyai_moe_route_hash(const flyai_moe_desc* desc, int32_t num_tokens, const void* x,
+                                   const int32_t* input_ids, const int32_t* tid2eid, int32_t vocab,
+                                   const flyai_moe_weights* w, void* logits, int32_t* topk_ids,
+                                   void* topk_weights, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
 /* Copy the routing plan flyai_moe_route left in the workspace: counts (int32
  * [El]) and exclusive offsets (int32 [El+1]) of this shard's experts, and the
  * permutation (int32 [M*k]): position p holds the flat pair index token*k+slot,
@@ -184,8 +226,8 @@ FLYAI_API int flyai_moe_read_plan(const flyai_moe_desc* desc, int32_t num_tokens
                         int32_t* perm, void* stream);
 
 /* Copy the error word kernels leave in the workspace (bit 1: a bounded wait gave
- * up; bit 2: a self-check -- enabled with FLYAI_MOE_CHECK=1 -- caught a bad
- * index) and 8 words of detail into out (device, int32 [9]); clear != 0 resets
+ * up; bit 2: a bad index -- a self-check enabled with FLYAI_MOE_CHECK=1, or a
+ * hash-routing input id or table entry out of range) and 8 words of detail into out (device, int32 [9]); clear != 0 resets
  * them.  Kernels never hang or trap on these conditions: they record and return. */
 FLYAI_API int flyai_moe_read_error(const flyai_moe_desc* desc, const void* workspace,
                                    size_t workspace_bytes, int32_t* out, int32_t clear,

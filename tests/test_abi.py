@@ -106,6 +106,29 @@ def test_nvfp4_prefill_workspace_limits():
     assert lib.flyai_moe_check_desc(ctypes.byref(fp8)) == _lib.ERR_UNSUPPORTED
 
 
+def test_v4_descriptor_validation():
+    lib = _lib.load()
+    ok = good_desc(format=_lib.FMT_FP4_W4A8, gating=_lib.GATE_SQRTSOFTPLUS, activation=_lib.ACT_SILU,
+                   num_experts=256, top_k=6, hidden=4096, inter=2048, expert_end=256,
+                   swiglu_limit=10.0, swiglu_alpha=0.0, n_group=1, topk_group=1, route_scale=1.5,
+                   n_shared=1)
+    assert lib.flyai_moe_check_desc(ctypes.byref(ok)) == _lib.OK
+    for kw, st in ((dict(gating=_lib.GATE_SIGMOID_GROUP), _lib.ERR_UNSUPPORTED),
+                   (dict(hidden=4096 + 64), _lib.ERR_ALIGNMENT),
+                   (dict(max_tokens=65), _lib.ERR_UNSUPPORTED),
+                   (dict(n_group=8), _lib.ERR_INVALID_ARG)):
+        d = _lib.Desc.from_buffer_copy(ok)
+        for k, v in kw.items():
+            setattr(d, k, v)
+        assert lib.flyai_moe_check_desc(ctypes.byref(d)) == st, kw
+    # bank: routed fp4 experts (0.5 B + 1/32 B per weight) then the fp8 shared expert
+    n = ctypes.c_size_t()
+    assert lib.flyai_moe_packed_bytes(ctypes.byref(ok), _lib.PROJ_W13, ctypes.byref(n)) == _lib.OK
+    routed = 256 * 2 * 2048 * 4096 * (0.5 + 1 / 32)
+    shared = 2 * 2048 * 4096 * (1 + 1 / 32)
+    assert n.value == int(routed + shared)
+
+
 def test_python_layer_refuses_cpu_device():
     import torch
     with pytest.raises((ValueError, RuntimeError)):
