@@ -6,7 +6,10 @@ top-4, H=I=2880), microseconds per layer, inputs resident in HBM, L2 flushed
 end through the public API with host buffers (H2D x, D2H y + router scores),
 the prefill chunk (config 2: M=2048, Zipf(1.1)-skewed router) in tokens/s, the
 roofline of the expert-streaming kernels, and the reference CPU path timed on
-this host.
+this host.  At N=1 the line also carries "families": the DeepSeek-V3 FP8 layer
+(config 3), the MiniMax-M2.5 NVFP4 layer (config 4, with its M=4096 prefill) and
+the DeepSeek-V4-Flash W4A8 layer, each with its verify-size sweep, expert-kernel
+roofline, end-to-end time and CPU oracle timing.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
@@ -43,10 +46,15 @@ def parse():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="flyai", choices=["flyai", "reference"])
-    p.add_argument("--workload", default="gptoss", choices=["gptoss", "dsv3", "m25"],
-                   help="gptoss: the headline (configs 1-2); dsv3: the DeepSeek-V3 FP8 layer "
-                        "(config 3); m25: the MiniMax-M2.5 NVFP4 layer (config 4, verify sizes)")
-    p.add_argument("--tokens", type=int, default=5)
+    p.add_argument("--workload", default="gptoss", choices=["gptoss", "dsv3", "m25", "v4"],
+                   help="gptoss: the headline (configs 1-2; at N=1 the line also carries the "
+                        "dsv3 / m25 / v4 layers as sub-objects); dsv3: the DeepSeek-V3 FP8 layer "
+                        "(config 3); m25: the MiniMax-M2.5 NVFP4 layer (config 4); v4: the "
+                        "DeepSeek-V4-Flash W4A8 layer")
+    p.add_argument("--tokens", type=int, default=None,
+                   help="verify-step tokens (default: 5; 1 for dsv3 and v4)")
+    p.add_argument("--no-families", action="store_true",
+                   help="default run: leave out the dsv3 / m25 / v4 sub-objects")
     p.add_argument("--prefill-tokens", type=int, default=None,
                    help="prefill chunk size (default: 2048 for gptoss, config 2; 4096 for m25, config 4)")
     p.add_argument("--no-prefill", action="store_true")
@@ -187,15 +195,22 @@ def cpu_layer_on_host(layer_dev, x_dev):
     return reference_layer_cpu(layer_cpu, x_dev.cpu())
 
 
-def time_cpu(fn, budget_s=20.0, max_calls=20):
-    fn()  # warm
+def time_cpu(fn, budget_s=20.0, max_calls=20, warm=1):
+    """Median seconds per call (and the min / max around it) over up to max_calls
+    calls within about budget_s -- the one statistic both CPU timings report."""
+    for _ in range(warm):
+        fn()
     times = []
     t_end = time.perf_counter() + budget_s
     while len(times) < max_calls and (not times or time.perf_counter() < t_end):
         t0 = time.perf_counter()
         fn()
         times.append(time.perf_counter() - t0)
-    return statistics.median(times), len(times)
+    return statistics.median(times), len(times), (min(times), max(times))
+
+
+def cpu_spread_us(spread):
+    return {"min_us": round(spread[0] * 1e6, 1), "max_us": round(spread[1] * 1e6, 1)}
 
 
 # ---------------------------------------------------------------------------
@@ -236,8 +251,10 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference_arm(args, world, rank)
-    if args.workload in ("dsv3", "m25"):
+    if args.workload in ("dsv3", "m25", "v4"):
         return main_dsv3(args, world, rank, local)
+    if args.tokens is None:
+        args.tokens = 5
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist = None
@@ -404,10 +421,21 @@ def main():
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         fn, kind = cpu_layer_on_host(layer, x)
-        t, n = time_cpu(fn)
+        t, n, spread = time_cpu(fn)
         result["cpu_baseline"] = {"value": round(t * 1e6, 1), "unit": "us", "cores": torch.get_num_threads(),
-                                  "kind": kind, "sample": f"{n} full layer calls at M={M} "
+                                  "kind": kind, "statistic": "median", **cpu_spread_us(spread),
+                                  "sample": f"{n} full layer calls at M={M} "
                                   "(router + touched experts; dequant to bf16 done once, untimed)"}
+    if world == 1 and not args.no_families:
+        # the other layer families of the path, each on its own (banks freed in between)
+        del moe
+        torch.cuda.empty_cache()
+        fam = {}
+        for wl in ("dsv3", "m25", "v4"):
+            fam[wl] = family_result(args, wl, 1, 0, dev, None, steps=20, warmup=3, sustain=0,
+                                    tokens=FAMILY_TOKENS[wl], compact=True)
+            torch.cuda.empty_cache()
+        result["families"] = fam
     if rank == 0:
         print(json.dumps(result), flush=True)
     if ep is not None:
@@ -417,49 +445,90 @@ def main():
         dist.destroy_process_group()
 
 
+FAMILY_TOKENS = {"dsv3": 1, "m25": 5, "v4": 1}
+
+
 def main_dsv3(args, world, rank, local):
-    """Config 3 (--workload dsv3): DeepSeek-V3-shaped FP8 layer (E=256 + 1 shared,
-    top-8 of 4/8 groups, H=7168, I=2048; 11.3 GB of banks).  Config 4 (--workload
-    m25): MiniMax-M2.5-shaped NVFP4 layer (E=256, top-8 sigmoid with a skewed
-    correction bias, H=3072, I=1536; 2.1 GB).  One GPU holds every expert;
-    microseconds per layer call at M=--tokens plus a sweep of verify sizes."""
-    from flyai_b200.moe import launch_count, set_profile_events
+    """--workload dsv3 | m25 | v4 on its own: one JSON line for that layer family
+    (expert parallel under torchrun: rank r holds experts [rE/N, (r+1)E/N))."""
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist = None
-    erange = None
-    if world > 1:   # expert parallel: rank r holds experts [rE/N, (r+1)E/N)
+    if world > 1:
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-        erange = (rank * 256 // world, (rank + 1) * 256 // world)
-    if args.workload == "dsv3":
+    tokens = args.tokens if args.tokens is not None else FAMILY_TOKENS[args.workload]
+    result = family_result(args, args.workload, world, rank, dev, dist, steps=args.steps,
+                           warmup=args.warmup, sustain=min(args.sustain, 500), tokens=tokens)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def family_result(args, workload, world, rank, dev, dist, steps, warmup, sustain, tokens, compact=False):
+    """Config 3 (dsv3): DeepSeek-V3-shaped FP8 layer (E=256 + 1 shared, top-8 of 4/8
+    groups, H=7168, I=2048; 11.3 GB of banks).  Config 4 (m25): MiniMax-M2.5-shaped
+    NVFP4 layer (E=256, top-8 sigmoid with a skewed correction bias, H=3072,
+    I=1536; 2.1 GB) with its M=4096 prefill batch.  v4: DeepSeek-V4-Flash W4A8 layer
+    (E=256 fp4 + 1 fp8 shared, top-6 sqrtsoftplus, H=4096, I=2048; 3.3 GB).  One GPU
+    holds every expert at N=1; microseconds per layer call at M=tokens plus a sweep
+    of verify sizes, the expert kernel alone, rooflines, and the CPU oracle port."""
+    from flyai_b200.moe import launch_count, set_profile_events
+    erange = (rank * 256 // world, (rank + 1) * 256 // world) if world > 1 else None
+    if workload == "dsv3":
         from flyai_b200.dsv3 import Fp8MoE
         from oracle import dsv3 as od
         layer = synth.make_dsv3_layer(**synth.DSV3, seed=args.seed, device=dev)
         moe = Fp8MoE.from_layer(layer, max_tokens=64, device=dev, expert_range=erange)
-        n_extra = 1   # the shared expert is read every call
         sweep_ms = (1, 8, 32)
-        metric = (f"MoE layer us at M={args.tokens} (DeepSeek-V3 FP8, E=256+1 shared, top-8 of 4/8 "
+        metric = (f"MoE layer us at M={tokens} (DeepSeek-V3 FP8, E=256+1 shared, top-8 of 4/8 "
                   "groups, H=7168, I=2048)")
         dtype = "e4m3 weights (fp32 128x128 scales) x e4m3 activations (fp32 1x128 scales), fp32 accumulate"
         cfg_extra = {"shared_experts": 1, "n_group": layer.n_group, "topk_group": layer.topk_group}
         kernel = "f8_moe_kernel (gate/up + down of one layer call, one launch)"
-        workload = f"deepseek-v3 fp8 MoE layer M={args.tokens} (config 3)"
-    else:
+        wl_name = f"deepseek-v3 fp8 MoE layer M={tokens} (config 3)"
+        data_cfg = "BASELINE config 3 distributions"
+
+        def kernel_bytes_of(distinct):
+            return (distinct + 1) * od.expert_bytes(Hd, Id)
+    elif workload == "m25":
         from flyai_b200.m25 import Nvfp4MoE
         from oracle import m25 as od
         layer = synth.make_m25_layer(**synth.M25, seed=args.seed, device=dev)
         moe = Nvfp4MoE.from_layer(layer, max_tokens=64, device=dev, expert_range=erange)
-        n_extra = 0
         sweep_ms = (1, 5, 16, 64)
-        metric = (f"MoE layer us at M={args.tokens} (MiniMax-M2.5 NVFP4, E=256 top-8 sigmoid, "
+        metric = (f"MoE layer us at M={tokens} (MiniMax-M2.5 NVFP4, E=256 top-8 sigmoid, "
                   "skewed, H=3072, I=1536)")
         dtype = ("nvfp4 weights (e2m1 + e4m3/16 + fp32 global) x bf16 activations as 6 e2m1 terms "
                  "(ue4m3/16), fp32 accumulate")
         cfg_extra = {"skew": "20% of experts take ~60% of picks (correction bias +0.14)"}
         kernel = "nv4_moe_kernel (gate/up + down of one layer call, one launch)"
-        workload = f"minimax-m2.5 nvfp4 MoE layer M={args.tokens} (config 4, verify size)"
+        wl_name = f"minimax-m2.5 nvfp4 MoE layer M={tokens} (config 4, verify size)"
+        data_cfg = "BASELINE config 4 distributions"
+
+        def kernel_bytes_of(distinct):
+            return distinct * od.expert_bytes(Hd, Id)
+    else:
+        from flyai_b200.v4 import W4A8MoE
+        from oracle import v4 as od
+        layer = synth.make_v4_layer(**synth.V4, seed=args.seed, device=dev)
+        moe = W4A8MoE.from_layer(layer, max_tokens=64, device=dev, expert_range=erange)
+        sweep_ms = (1, 6, 32, 64)
+        metric = (f"MoE layer us at M={tokens} (DeepSeek-V4-Flash W4A8, E=256 fp4 + 1 fp8 shared, "
+                  "top-6 sqrtsoftplus, H=4096, I=2048)")
+        dtype = ("e2m1 weights (e8m0/32) x e4m3 activations (ue8m0 1x128), shared expert e4m3 "
+                 "(e8m0 128x128), fp32 accumulate")
+        cfg_extra = {"shared_experts": 1, "swiglu_limit": layer.swiglu_limit,
+                     "route_scale": layer.route_scale}
+        kernel = "v4_moe_kernel (gate/up + down of routed and shared experts, one launch)"
+        wl_name = f"deepseek-v4-flash w4a8 MoE layer M={tokens} (decode)"
+        data_cfg = "V4-Flash config.json shapes, config 0 value distributions"
+
+        def kernel_bytes_of(distinct):
+            return distinct * od.expert_bytes(Hd, Id) + od.shared_bytes(Hd, Id)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     Hd, Id, Ed, Kd = layer.hidden, layer.inter, layer.num_experts, layer.top_k
     hbm_peak, peak_kind = peaks()
@@ -480,6 +549,9 @@ def main_dsv3(args, world, rank, local):
         t = torch.tensor([v], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    def touched(ids_np):   # the layer's algorithmic bytes: experts, router, x and y
+        return od.touched_bytes(ids_np, ids_np.shape[0], Hd, Id, Ed)
 
     def measure(M, steps, warmup, sampler=None, sustain=0):
         x = synth.make_tokens(M, Hd, seed=args.seed + M, device=dev)
@@ -519,23 +591,24 @@ def main_dsv3(args, world, rank, local):
         lo, hi = erange if erange is not None else (0, Ed)
         local = len(set(v for v in ids_np.ravel().tolist() if lo <= v < hi))
         # bytes the busiest rank's expert kernel streams (the kernel time is the max over ranks)
-        kbytes = (distinct + n_extra) * od.expert_bytes(Hd, Id)
+        kbytes = kernel_bytes_of(distinct)
         if dist is not None:
-            t = torch.tensor([(local + (n_extra if lo == 0 else 0)) * od.expert_bytes(Hd, Id)],
-                             device=dev, dtype=torch.float64)
+            mine = kernel_bytes_of(local) if lo == 0 else kernel_bytes_of(local) - kernel_bytes_of(0)
+            t = torch.tensor([mine], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             kbytes = int(t.item())
-        lbytes = od.touched_bytes(ids_np, M, Hd, Id, Ed)
+        lbytes = touched(ids_np)
         return dict(x=x, y=y, ms=ms, kms=kms, launches=launches, distinct=distinct,
                     kernel_bytes=kbytes, layer_bytes=lbytes, ids=ids_np)
 
-    M = args.tokens
-    sampler = ClockSampler(local)
-    head = measure(M, args.steps, args.warmup, sampler, sustain=min(args.sustain, 500))
+    M = tokens
+    sampler = ClockSampler(dev.index)
+    head = measure(M, steps, warmup, sampler, sustain=sustain)
     clocks = sampler.summary()
+    assert moe.read_error()[0] == 0
     sweep = {}
     for m in sweep_ms:
-        r = head if m == M else measure(m, max(10, args.steps // 2), args.warmup)
+        r = head if m == M else measure(m, max(10, steps // 2), warmup)
         sweep[str(m)] = {"us": round(r["ms"] * 1e3, 2), "kernel_us": round(r["kms"] * 1e3, 2),
                          "distinct_experts": r["distinct"],
                          "layer_hbm_frac": round(r["layer_bytes"] / (r["ms"] * 1e-3) / 1e9 / world / hbm_peak, 4),
@@ -545,13 +618,13 @@ def main_dsv3(args, world, rank, local):
     y_h = torch.empty_like(x_h).pin_memory()
     x_in = torch.empty_like(head["x"])
     y = head["y"]
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         x_in.copy_(x_h, non_blocking=True)
         layer_step(x_in, y)
         y_h.copy_(y, non_blocking=True)
     torch.cuda.synchronize()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    for i in range(args.steps):
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
         flush.zero_()
         ev[i][0].record()
         x_in.copy_(x_h, non_blocking=True)
@@ -559,15 +632,15 @@ def main_dsv3(args, world, rank, local):
         y_h.copy_(y, non_blocking=True)
         ev[i][1].record()
     torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) / args.steps)
+    e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) / steps)
     achieved = head["kernel_bytes"] / (head["kms"] * 1e-3) / 1e9
     result = {
         "metric": metric,
-        "value": round(head["ms"] * 1e3, 2), "unit": "us", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(head["ms"], 5), "higher_is_better": False,
+        "value": round(head["ms"] * 1e3, 2), "unit": "us", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(head["ms"], 5), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": dtype,
-        "data": f"synthetic (seeded; BASELINE config {3 if args.workload == 'dsv3' else 4} distributions)",
-        "config": {"workload": workload, "experts": Ed, "top_k": Kd, "hidden": Hd, "inter": Id,
+        "data": f"synthetic (seeded; {data_cfg})",
+        "config": {"workload": wl_name, "experts": Ed, "top_k": Kd, "hidden": Hd, "inter": Id,
                    "tokens": M, "parallelism": f"ep{world}",
                    "l2": "flushed (256 MiB write) before every timed step", **cfg_extra},
         "e2e": {"value": round(e2e_ms * 1e3, 2), "unit": "us", "h2d_bytes_per_step": M * Hd * 2,
@@ -582,12 +655,12 @@ def main_dsv3(args, world, rank, local):
                      "layer_hbm_frac": round(head["layer_bytes"] / (head["ms"] * 1e-3) / 1e9 / world / hbm_peak, 4)},
         "sweep": sweep,
     }
-    if args.workload == "m25" and not args.no_prefill:
+    if workload == "m25" and not args.no_prefill:
         result["prefill"] = m25_prefill(args, layer, erange, world, dev, flush, max_over_ranks, hbm_peak)
     if not args.no_cpu_baseline and rank == 0 and world == 1:
         xc = head["x"].float().cpu().numpy()
         rw, rb = layer.router_w.float().cpu().numpy(), layer.bias.cpu().numpy()
-        if args.workload == "dsv3":
+        if workload == "dsv3":
             cache = {}
 
             def get(e):
@@ -601,7 +674,7 @@ def main_dsv3(args, world, rank, local):
                 ids, wts, _ = od.gate(xc, rw, rb, Kd, layer.n_group, layer.topk_group, layer.route_scale)
                 return od.moe_forward(xc, ids, wts, get, Ed)
             note = "gate + touched experts + shared, fp8 dequant inside the timed call"
-        else:
+        elif workload == "m25":
             cache = {}
 
             def get(e):
@@ -619,15 +692,33 @@ def main_dsv3(args, world, rank, local):
                 return od.moe_forward(xc, ids, wts, get)
             fn()   # dequantise the touched experts once, outside the timing
             note = "router + touched experts, NVFP4 dequant to bf16 done once, untimed"
-        t, n = time_cpu(fn, budget_s=20.0, max_calls=5)
+        else:
+            cache = {}
+
+            def get(e):
+                if e not in cache:
+                    cache[e] = tuple(t.cpu().numpy() for t in layer.expert(e))
+                return cache[e]
+            sw = layer.shared()
+            shared_np = (sw[0].view(torch.uint8).cpu().numpy(), sw[1].cpu().numpy(),
+                         sw[2].view(torch.uint8).cpu().numpy(), sw[3].cpu().numpy())
+
+            def fn():
+                ids, wts, _ = od.gate(xc, rw, rb, Kd, layer.route_scale)
+                return od.moe_forward(xc, ids, wts, get, lambda: shared_np, layer.swiglu_limit)
+            note = "gate + touched fp4 experts + fp8 shared expert, dequant inside the timed call"
+        t, n, spread = time_cpu(fn, budget_s=20.0, max_calls=5)
         result["cpu_baseline"] = {"value": round(t * 1e6, 1), "unit": "us", "cores": torch.get_num_threads(),
-                                  "kind": "port", "sample": f"{n} full layer calls at M={M} (numpy oracle: "
-                                  f"{note})"}
-    if rank == 0:
-        print(json.dumps(result), flush=True)
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
+                                  "kind": "port", "statistic": "median", **cpu_spread_us(spread),
+                                  "sample": f"{n} full layer calls at M={M} (numpy oracle: {note})"}
+    if ep is not None:
+        del ep
+    del moe
+    if compact:
+        keep = ("metric", "value", "unit", "dtype", "config", "e2e", "gpu_launches", "roofline",
+                "sweep", "prefill", "cpu_baseline")
+        result = {k: v for k, v in result.items() if k in keep}
+    return result
 
 
 def m25_prefill(args, layer, erange, world, dev, flush, max_over_ranks, hbm_peak):
@@ -713,6 +804,8 @@ def run_reference_arm(args, world, rank):
     """The reference's own CPU implementation, timed on this host's cores."""
     if rank != 0:
         return
+    if args.tokens is None:
+        args.tokens = 5
     layer = synth.make_gpt_oss_layer(**synth.GPT_OSS_120B, seed=args.seed)
     x = synth.make_tokens(args.tokens, H, seed=args.seed)
     fn, kind = reference_layer_cpu(layer, x)
@@ -725,7 +818,9 @@ def run_reference_arm(args, world, rank):
         per_step.append(time.perf_counter() - t0)
         if sum(per_step) > 120:
             break
-    us = statistics.mean(per_step) * 1e6
+    # the median (with its spread), the statistic the GPU arm's cpu_baseline reports
+    us = statistics.median(per_step) * 1e6
+    spread = (min(per_step), max(per_step))
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us",
         "n_gpus": world, "steps": len(per_step), "warmup": args.warmup,
@@ -736,7 +831,8 @@ def run_reference_arm(args, world, rank):
                    "top_k": K_TOP, "hidden": H, "inter": I, "tokens": args.tokens,
                    "parallelism": "cpu"},
         "cpu_baseline": {"value": round(us, 1), "unit": "us", "cores": torch.get_num_threads(),
-                         "kind": kind, "sample": f"{len(per_step)} layer calls at M={args.tokens}, "
+                         "kind": kind, "statistic": "median", **cpu_spread_us(spread),
+                         "sample": f"{len(per_step)} layer calls at M={args.tokens}, "
                          "transformers eager router+experts on CPU, dequant untimed"},
         "e2e": {"value": round(us, 1), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)

@@ -145,10 +145,12 @@ static int launch_layer_experts(const flyai_moe_desc& d, int M, const void* x,
 
 static int launch_layer_route(const flyai_moe_desc& d, int M, const void* x,
                               const flyai_moe_weights& w, float* logits, int32_t* topk_ids,
-                              float* topk_weights, const Fp8Workspace& fw, cudaStream_t s) {
+                              float* topk_weights, const Fp8Workspace& fw, cudaStream_t s,
+                              const void* logits_in = nullptr) {
   if (d.format == FLYAI_FMT_NVFP4 && M > kF8MaxTokens)
-    return launch_nvp_route(d, M, x, w, logits, topk_ids, topk_weights, fw, s);
-  return launch_fp8_route(d, M, x, w, logits, topk_ids, topk_weights, fw, s);
+    return launch_nvp_route(d, M, x, w, logits, topk_ids, topk_weights, fw, s, logits_in);
+  return launch_fp8_route(d, M, x, w, logits, topk_ids, topk_weights, fw, s, nullptr, nullptr, 0,
+                          logits_in);
 }
 
 // Expert projections: the tcgen05 block-scaled kernels (every MXFP4 descriptor
@@ -313,6 +315,22 @@ int flyai_moe_route_hash(const flyai_moe_desc* desc, int32_t M, const void* x, c
   return launch_fp8_route(*desc, M, x, *w, static_cast<float*>(logits), topk_ids,
                           static_cast<float*>(topk_weights), fw, static_cast<cudaStream_t>(stream),
                           tid2eid, input_ids, vocab);
+}
+
+int flyai_moe_route_logits(const flyai_moe_desc* desc, int32_t M, const void* x,
+                           const void* router_logits, const flyai_moe_weights* w, int32_t* topk_ids,
+                           void* topk_weights, void* workspace, size_t workspace_bytes, void* stream) {
+  FLYAI_TRY(check_desc(desc));
+  FLYAI_TRY(check_tokens(desc, M));
+  FLYAI_TRY(check_workspace(desc, workspace, workspace_bytes));
+  FLYAI_TRY(check_weights(desc, w, true, false));
+  if (desc->gating != FLYAI_GATE_SIGMOID_BF16) return FLYAI_ERR_UNSUPPORTED;
+  if (M > 0 && (!x || !router_logits)) return FLYAI_ERR_INVALID_ARG;
+  if ((x && !aligned(x, 16)) || (router_logits && !aligned(router_logits, 16))) return FLYAI_ERR_ALIGNMENT;
+  if (!w->router_b || !aligned(w->router_b, 4)) return FLYAI_ERR_INVALID_ARG;
+  const Fp8Workspace fw = carve_fp8_workspace(*desc, desc->max_tokens, workspace);
+  return launch_layer_route(*desc, M, x, *w, nullptr, topk_ids, static_cast<float*>(topk_weights), fw,
+                            static_cast<cudaStream_t>(stream), router_logits);
 }
 
 int flyai_moe_read_plan(const flyai_moe_desc* desc, int32_t M, const void* workspace,

@@ -170,6 +170,10 @@ struct F8RouteParams {
   const int32_t* input_ids;  // [M] (with tid2eid)
   int vocab;
   int ue8m0;             // act_quant scales 2^ceil(log2(amax/448)) (scale_fmt "ue8m0")
+  // bf16 [M, E] router logits the caller computed (MiniMax-M2.5's stage passes
+  // F.linear(h, gate) to its FusedMoE): the selection reads these instead of the
+  // kernel's own (which still runs for the token-row factors)
+  const uint16_t* logits_in;
   int32_t* err;          // error word (bit 2: an input id or table entry out of range)
 };
 
@@ -297,7 +301,8 @@ __device__ void f8_select_token(const F8RouteParams& p, int t, KV* row, void* tk
     ch[j] = -INFINITY;
     if (j < nj) {
       const int e = lane * nj + j;
-      const float l = __ldcg(p.logits + static_cast<size_t>(t) * E + e);
+      const float l = p.logits_in ? __uint_as_float(static_cast<uint32_t>(__ldg(p.logits_in + static_cast<size_t>(t) * E + e)) << 16)
+                                  : __ldcg(p.logits + static_cast<size_t>(t) * E + e);
       const float s = f8_score(p.score_fn, l);
       sc[j] = s;
       ch[j] = __fadd_rn(s, __ldg(p.bias + e));
@@ -371,10 +376,23 @@ __device__ void f8_select_token(const F8RouteParams& p, int t, KV* row, void* tk
 // sorted=False order, as in f8_select_token.
 __device__ void f8_select_token_256(const F8RouteParams& p, int t, KV* row, void* tks) {
   const int lane = threadIdx.x & 31, k = p.k;
-  const float4* lg = reinterpret_cast<const float4*>(p.logits + static_cast<size_t>(t) * 256 + lane * 8);
   const float4* bs = reinterpret_cast<const float4*>(p.bias + lane * 8);
-  const float4 l0 = __ldcg(lg), l1 = __ldcg(lg + 1), b0 = __ldg(bs), b1 = __ldg(bs + 1);
-  const float lv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+  const float4 b0 = __ldg(bs), b1 = __ldg(bs + 1);
+  float lv[8];
+  if (p.logits_in) {
+    const uint4 r = __ldg(reinterpret_cast<const uint4*>(p.logits_in + static_cast<size_t>(t) * 256 + lane * 8));
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      lv[2 * j] = __uint_as_float(w[j] << 16);
+      lv[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    }
+  } else {
+    const float4* lg = reinterpret_cast<const float4*>(p.logits + static_cast<size_t>(t) * 256 + lane * 8);
+    const float4 l0 = __ldcg(lg), l1 = __ldcg(lg + 1);
+    lv[0] = l0.x, lv[1] = l0.y, lv[2] = l0.z, lv[3] = l0.w;
+    lv[4] = l1.x, lv[5] = l1.y, lv[6] = l1.z, lv[7] = l1.w;
+  }
   const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
   float sc[8], ch[8];
 #pragma unroll
@@ -715,9 +733,10 @@ __global__ void __launch_bounds__(kF8RouteThreads, kNv ? 1 : 2) f8_route_kernel(
 int launch_fp8_route(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_weights& w,
                      float* logits, int32_t* topk_ids, float* topk_weights,
                      const Fp8Workspace& ws, cudaStream_t stream, const int32_t* tid2eid,
-                     const int32_t* input_ids, int vocab) {
+                     const int32_t* input_ids, int vocab, const void* logits_in) {
   if (M == 0) return FLYAI_OK;
   F8RouteParams prm{};
+  prm.logits_in = static_cast<const uint16_t*>(logits_in);
   prm.score_fn = d.gating == FLYAI_GATE_SQRTSOFTPLUS ? 1 : 0;
   prm.sorted = d.gating == FLYAI_GATE_SQRTSOFTPLUS ? 1 : 0;
   prm.ue8m0 = is_v4(d) ? 1 : 0;
@@ -779,9 +798,11 @@ __global__ void __launch_bounds__(256) f8_select_kernel(const __grid_constant__ 
 
 int launch_fp8_select(const flyai_moe_desc& d, int M, const flyai_moe_weights& w,
                       int32_t* topk_ids, float* topk_weights, const Fp8Workspace& ws,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, const void* logits_in) {
   if (M == 0) return FLYAI_OK;
   F8RouteParams prm{};
+  prm.logits_in = static_cast<const uint16_t*>(logits_in);
+  prm.err = ws.err;
   prm.bias = static_cast<const float*>(w.router_b);
   prm.M = M;
   prm.E = d.num_experts;

@@ -164,11 +164,14 @@ int launch_fp8_pack(const flyai_moe_desc& d, int proj, const void* weight, const
 // Gate (grouped sigmoid, or the bf16-logit sigmoid gate of FLYAI_GATE_SIGMOID_BF16)
 // + token rows quantised (FP8) or split into terms (NVFP4) + routing plan;
 // logits/ids/weights outputs may be null.
-// tid2eid / input_ids / vocab: a hash-routed layer (FLYAI_GATE_SQRTSOFTPLUS).
+// tid2eid / input_ids / vocab: a hash-routed layer (FLYAI_GATE_SQRTSOFTPLUS);
+// logits_in: bf16 [M, E] logits the caller computed, selected from instead of the
+// kernel's own (FLYAI_GATE_SIGMOID_BF16).
 int launch_fp8_route(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_weights& w,
                      float* logits, int32_t* topk_ids, float* topk_weights,
                      const Fp8Workspace& ws, cudaStream_t stream, const int32_t* tid2eid = nullptr,
-                     const int32_t* input_ids = nullptr, int vocab = 0);
+                     const int32_t* input_ids = nullptr, int vocab = 0,
+                     const void* logits_in = nullptr);
 size_t nv4_packed_bytes(const flyai_moe_desc& d, int proj);
 int launch_nv4_pack(const flyai_moe_desc& d, int proj, const void* blocks, const void* scales,
                     const void* global_scale, void* packed, cudaStream_t stream);
@@ -188,13 +191,13 @@ int launch_fp8_combine(const flyai_moe_desc& d, int M, const uint16_t* rows, voi
 // Selection alone (f8_route_kernel's per-token step) on the logits in ws.logits.
 int launch_fp8_select(const flyai_moe_desc& d, int M, const flyai_moe_weights& w,
                       int32_t* topk_ids, float* topk_weights, const Fp8Workspace& ws,
-                      cudaStream_t stream);
+                      cudaStream_t stream, const void* logits_in = nullptr);
 // NVFP4 prefill (M > kF8MaxTokens): router logits, selection, plan of kNpChunk-pair
 // chunks and the chunks' bf16 token rows; then the expert kernel (and the fold
 // into y when y is not null).
 int launch_nvp_route(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_weights& w,
                      float* logits, int32_t* topk_ids, float* topk_weights,
-                     const Fp8Workspace& ws, cudaStream_t stream);
+                     const Fp8Workspace& ws, cudaStream_t stream, const void* logits_in = nullptr);
 int launch_nvp_experts(const flyai_moe_desc& d, int M, const flyai_moe_weights& w, void* y,
                        uint16_t* rows, const Fp8Workspace& ws, cudaStream_t stream,
                        cudaEvent_t ev0, cudaEvent_t ev1);

@@ -785,7 +785,7 @@ __global__ void __launch_bounds__(kNpThreads, 1) nvp_moe_kernel(const __grid_con
 // ---------------------------------------------------------------------------
 int launch_nvp_route(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_weights& w,
                      float* logits, int32_t* topk_ids, float* topk_weights,
-                     const Fp8Workspace& ws, cudaStream_t stream) {
+                     const Fp8Workspace& ws, cudaStream_t stream, const void* logits_in) {
   if (M == 0) return FLYAI_OK;
   const int E = d.num_experts, H = d.hidden, k = d.top_k;
   const int El = d.expert_end - d.expert_begin;
@@ -801,7 +801,7 @@ int launch_nvp_route(const flyai_moe_desc& d, int M, const void* x, const flyai_
                 ws.logits, logits, ws.pxr) != cudaSuccess)
     return FLYAI_ERR_CUDA;
   note_launch();
-  const int st = launch_fp8_select(d, M, w, topk_ids, topk_weights, ws, stream);
+  const int st = launch_fp8_select(d, M, w, topk_ids, topk_weights, ws, stream, logits_in);
   if (st != FLYAI_OK) return st;
   NpPlanParams pp{ws.ids, M * k, d.expert_begin, El, ws.max_chunks, ws.counts, ws.offsets, ws.perm,
                   ws.inv, ws.n_chunks, ws.chunk_info, ws.chunk_done};

@@ -30,6 +30,8 @@ ENABLED = os.environ.get("FLYAI_MOE_B200", "0") == "1"
 
 _LOCK = threading.Lock()
 _COVERAGE = Counter()
+_INSTALLED = []   # mlp modules whose forward this lever rebound
+_ATTEMPTS = [0]   # install() calls
 
 
 def coverage():
@@ -98,7 +100,10 @@ def install(layers, banks, max_tokens=64, return_logits=False):
 
     ``banks[i]`` is the dict of checkpoint tensors of layer i (keys as
     ``B200GptOssMLP.from_checkpoint`` arguments).  Returns the installed
-    modules.  The previous forward of each mlp stays reachable as the fallback."""
+    modules.  The previous forward of each mlp stays reachable as the fallback.
+    Stage code calls this when FLYAI_MOE_B200=1 (``ENABLED``); the lever registry
+    (flyai_b200.levers) reports a call made with the flag off."""
+    _ATTEMPTS[0] += 1
     installed = []
     for layer, bank in zip(layers, banks):
         mlp = layer.mlp
@@ -112,4 +117,16 @@ def install(layers, banks, max_tokens=64, return_logits=False):
         fwd.__func__._flyai_b200 = True
         mlp.forward = fwd
         installed.append(mod)
+        with _LOCK:
+            _INSTALLED.append(mlp)
     return installed
+
+
+def attempts():
+    return _ATTEMPTS[0]
+
+
+def installed_count():
+    """mlp modules whose forward is this lever right now."""
+    with _LOCK:
+        return sum(1 for m in _INSTALLED if getattr(m.forward, "_flyai_b200", False))

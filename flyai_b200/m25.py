@@ -5,14 +5,17 @@ one device, with the reference's operator surface:
 
 * ``route(x)``   -> (logits fp32 holding bf16 values, topk_idx, topk_weight) --
   MiniMaxM2TopKRouter.forward (transformers/models/minimax_m2/modeling_minimax_m2.py;
-  ids in descending choice score rather than torch's unsorted order)
-* ``forward(x)`` -> y bf16 -- MiniMaxM2SparseMoeBlock.forward, the layer the M2.5
-  stage calls as ``self.moe(h, logits)`` (engines/minimax_m25/m25_stage.py:412-416)
+  ids in torch.topk(sorted=False)'s CPU order)
+* ``forward(x)`` -> y bf16 -- MiniMaxM2SparseMoeBlock.forward
+* ``self(h, router_logits)`` -> y bf16 -- the FusedMoE call of the M2.5 stage,
+  ``self.moe(h, rl)`` with rl = F.linear(h, gate) computed by the caller
+  (engines/minimax_m25/m25_stage.py:412-416): routes from the passed logits
 
 Stream-ordered on torch's current CUDA stream, no host synchronisation and no
 allocation after construction.
 """
 import ctypes
+import os
 
 import torch
 
@@ -106,3 +109,62 @@ class Nvfp4MoE(Fp8MoE):
         rb = (I if proj == _lib.PROJ_W13 else H) // 128
         kb = (H if proj == _lib.PROJ_W13 else I) // 128
         return tiles * (128 * 64 + 2 * 512) * rb * kb
+
+    def fused_moe(self, hidden_states, router_logits=None, out=None):
+        """The M2.5 stage's ``self.moe(h, router_logits)``: routed from the caller's bf16
+        logits [M, E] (flyai_moe_route_logits), or from the layer's own router when
+        they are None."""
+        if router_logits is None:
+            return Fp8MoE.forward(self, hidden_states, out=out)
+        self._check_x(hidden_states)
+        M = hidden_states.shape[0]
+        rl = router_logits.to(device=self.device, dtype=torch.bfloat16).contiguous()
+        if rl.shape != (M, self.num_experts):
+            raise ValueError(f"router_logits must be [M, {self.num_experts}]")
+        y = out if out is not None else torch.empty_like(hidden_states)
+        with torch.cuda.device(self.device):
+            _lib.call("flyai_moe_route_logits", ctypes.byref(self.desc), M, _ptr(hidden_states), _ptr(rl),
+                      ctypes.byref(self.weights), None, None, _ptr(self.workspace),
+                      self.workspace.numel(), _stream())
+            _lib.call("flyai_moe_experts", ctypes.byref(self.desc), M, _ptr(hidden_states),
+                      ctypes.byref(self.weights), _ptr(y), _ptr(self.workspace),
+                      self.workspace.numel(), _stream())
+        return y
+
+    __call__ = fused_moe
+
+
+# ---- the M2.5 stage lever ---------------------------------------------------
+ENABLED = os.environ.get("FLYAI_MOE_M25", "1") not in ("", "0")
+_INSTALLED = []
+_ATTEMPTS = [0]
+
+
+def install(layers, build):
+    """Replace each M2.5 stage layer's FusedMoE -- ``layer.moe``, which the stage
+    calls as ``self.moe(h, router_logits)`` (engines/minimax_m25/m25_stage.py:
+    412-416) -- by the ``Nvfp4MoE`` that ``build(layer)`` returns (built from the
+    layer's ModelOpt NVFP4 tensors).  The replaced module stays reachable as
+    ``layer._flyai_prev_moe``.  A no-op with FLYAI_MOE_M25=0.  Returns the number
+    of layers replaced."""
+    _ATTEMPTS[0] += 1
+    if not ENABLED:
+        return 0
+    n = 0
+    for layer in layers:
+        if isinstance(layer.moe, Nvfp4MoE):
+            continue
+        layer._flyai_prev_moe = layer.moe
+        layer.moe = build(layer)
+        _INSTALLED.append(layer)
+        n += 1
+    return n
+
+
+def attempts():
+    return _ATTEMPTS[0]
+
+
+def installed():
+    """Stage layers whose ``moe`` is this lever's module right now."""
+    return [layer for layer in _INSTALLED if isinstance(layer.moe, Nvfp4MoE)]

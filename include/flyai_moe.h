@@ -215,6 +215,17 @@ FLYAI_API int flyai_moe_route_hash(const flyai_moe_desc* desc, int32_t num_token
                                    void* topk_weights, void* workspace, size_t workspace_bytes,
                                    void* stream);
 
+/* Router of a MiniMax-M2 layer from logits the caller computed: the M2.5 stage
+ * computes rl = F.linear(h, gate) (bf16 [M, E]) and hands (h, rl) to its FusedMoE
+ * (engines/minimax_m25/m25_stage.py:412-416); this selects from rl -- sigmoid,
+ * correction bias, top-k, renormalise -- and builds the plan and token rows as
+ * flyai_moe_route does.  FLYAI_GATE_SIGMOID_BF16 descriptors; then
+ * flyai_moe_experts. */
+FLYAI_API int flyai_moe_route_logits(const flyai_moe_desc* desc, int32_t num_tokens, const void* x,
+                                     const void* router_logits, const flyai_moe_weights* w,
+                                     int32_t* topk_ids, void* topk_weights, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
 /* Copy the routing plan flyai_moe_route left in the workspace: counts (int32
  * [El]) and exclusive offsets (int32 [El+1]) of this shard's experts, and the
  * permutation (int32 [M*k]): position p holds the flat pair index token*k+slot,
