@@ -56,18 +56,6 @@ __device__ __forceinline__ void e2m1x8_to_f16x8(uint32_t w, uint32_t& r0, uint32
       : "r"(w));
 }
 
-// D = A(16x16 f16, row) * B(16x8 f16, col) + C (fp32), warp-wide.
-__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                          uint32_t a3, uint32_t b0, uint32_t b1,
-                                          const float (&c)[4]) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};\n"
-      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]),
-        "f"(c[2]), "f"(c[3]));
-}
-
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   uint4 r;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
@@ -215,24 +203,21 @@ constexpr int kEpFlagBytes = 256;
 constexpr int kEpFailWord = 16;
 
 constexpr int kTcChunk = 4;      // tokens of one expert per chunk, tcgen05 verify kernel
-constexpr int kTcPrefillChunk = 16;   // tokens per chunk, tcgen05 prefill kernel
+constexpr int kTcPfChunk = 128;   // pairs per chunk, tcgen05 prefill kernel (the MMA's N)
 constexpr int kTcPrefillMinTokens = 65;   // batches this large take the prefill kernel
-constexpr int kChunkRowStride = 16;   // token-row slots per chunk descriptor
-// Tokens per chunk of the tcgen05 kernels for a batch of M tokens.
+constexpr int kTcPfK = 64;          // K elements per bf16 row slice of the prefill kernel
+constexpr int kTcPfBlk = kTcPfChunk * kTcPfK * 2;   // 16 KB: one slice of a full chunk
+constexpr int kChunkRowStride = 16;   // token-row slots per chunk descriptor (verify chunks)
+// Pairs per chunk of the tcgen05 kernels for a batch of M tokens.
 __host__ __device__ inline int tc_chunk_tokens(int M) {
-  return M >= kTcPrefillMinTokens ? kTcPrefillChunk : kTcChunk;
+  return M >= kTcPrefillMinTokens ? kTcPfChunk : kTcChunk;
+}
+// Upper bound on the prefill chunks of P pairs over El experts: every non-empty
+// expert has one partial chunk at most.
+__host__ __device__ inline int tc_pf_max_chunks(size_t P, size_t El) {
+  return static_cast<int>((El < P ? El : P) + P / kTcPfChunk + 1);
 }
 constexpr int kTerms = 6;        // e2m1 terms an activation row is split into for kind::mxf4
-// Prefill layout of a term row: cut into 512-element K-tiles of 16 blocks, tile
-// kt of position pos at (kt * pstride + pos) * term_ktile_bytes(), so the rows
-// of consecutive positions for one K-tile are one contiguous run.
-constexpr int kTermTileBlocks = 16;
-__host__ __device__ inline size_t term_ktile_bytes() {
-  return static_cast<size_t>(kTermTileBlocks) * kTerms * 16;
-}
-__host__ __device__ inline size_t term_ktile_row_bytes(int K) {
-  return static_cast<size_t>((K / 32 + kTermTileBlocks - 1) / kTermTileBlocks) * term_ktile_bytes();
-}
 
 // ---- workspace layout -------------------------------------------------------
 // All regions 256-byte aligned, carved in this order from the caller's buffer.
@@ -245,7 +230,6 @@ struct Workspace {
   int32_t* active;     // [E_local]  local expert index of each non-empty expert
   int32_t* n_active;   // [1]
   int32_t* perm;       // [M*k] flat pair index at each permuted position
-  uint16_t* hbuf;      // [M*k, I] bf16 SwiGLU output, permuted order
   uint16_t* pair_out;  // [M*k, H] bf16 weighted expert outputs, flat pair order
   int32_t* err;        // [1] error bits set by kernels (kErr*)
   int32_t* dbg;        // [8] first failure details of the self-checking build
@@ -256,17 +240,18 @@ struct Workspace {
                          //     before first use, restored to 0 by every call
   int32_t* fold_ticket;  // [M * H/16] contributions per (token, 16-row output tile);
                          //     cleared by the route step of every call
-  int32_t* n_chunks;   // [1] number of chunks (kTokChunk or kTcChunk tokens) over all non-empty experts
+  int32_t* n_chunks;   // [1] number of chunks (tc_chunk_tokens pairs each) over all non-empty experts
   int32_t* chunk_slot; // [max_chunks] active-list slot of each chunk
   int32_t* chunk_c0;   // [max_chunks] first token (within the expert) of each chunk
   uint8_t* x_terms;    // [M][H/32][kTerms][16] e2m1 terms of every token row (tensor-core path)
   uint8_t* x_sf;       // [M][H/128][8][4] their e8m0 scales
   uint8_t* h_terms;    // [M*k][I/32][kTerms][16] terms of the SwiGLU rows, permuted order
-                       // (prefill batches: K-tile major, see term_ktile_bytes)
   uint8_t* h_sf;       // [M*k][I/128][8][4]
-  uint8_t* x_pterms;   // prefill only: x terms by permuted position, K-tile major
-  uint8_t* x_psf;      // prefill only: their scales [M*k][H/128][8][4]
-  int pstride;         // positions per K-tile of the K-tile-major term layouts (= M*k)
+  uint8_t* pxb;        // prefill only: [pf_max_chunks][H/64][kTcPfBlk] bf16 token rows by chunk
+  uint8_t* phb;        // prefill only: [pf_max_chunks][I/64][kTcPfBlk] bf16 SwiGLU rows by chunk
+  int32_t* pcf;        // prefill only: [pf_max_chunks][kTcPfChunk] flat pair index per chunk slot
+  float* pcw;          // prefill only: [pf_max_chunks][kTcPfChunk] routing weight per chunk slot
+  int pf_max_chunks;
   int4* chunk_info;    // [max_chunks] (local expert, first permuted position, tokens, 0)
   int32_t* chunk_rows; // [max_chunks][kChunkRowStride] token row of each of the chunk's tokens
   int32_t* chunk_done; // [max_chunks] gate/up tiles of the chunk finished (cleared by route)
@@ -298,7 +283,6 @@ inline Workspace carve_workspace(const flyai_moe_desc& d, int M, void* base) {
   w.active = reinterpret_cast<int32_t*>(take(El * 4));
   w.n_active = reinterpret_cast<int32_t*>(take(4));
   w.perm = reinterpret_cast<int32_t*>(take(P * 4));
-  w.hbuf = reinterpret_cast<uint16_t*>(take(P * static_cast<size_t>(d.inter) * 2));
   w.pair_out = reinterpret_cast<uint16_t*>(take(P * static_cast<size_t>(d.hidden) * 2));
   w.err = reinterpret_cast<int32_t*>(take(4));
   w.dbg = reinterpret_cast<int32_t*>(take(32));
@@ -309,18 +293,20 @@ inline Workspace carve_workspace(const flyai_moe_desc& d, int M, void* base) {
   w.chunk_c0 = reinterpret_cast<int32_t*>(take(static_cast<size_t>(w.max_chunks) * 4));
   const size_t sfh = static_cast<size_t>((d.hidden + 127) / 128) * 32;
   const size_t sfi = static_cast<size_t>((d.inter + 127) / 128) * 32;
-  w.x_terms = reinterpret_cast<uint8_t*>(take(static_cast<size_t>(M) * kTerms * (d.hidden / 2)));
-  w.x_sf = reinterpret_cast<uint8_t*>(take(static_cast<size_t>(M) * sfh));
-  const bool prefill = M >= kTcPrefillMinTokens;
-  const size_t hrow = prefill && term_ktile_row_bytes(d.inter) > static_cast<size_t>(kTerms) * (d.inter / 2)
-                          ? term_ktile_row_bytes(d.inter)
-                          : static_cast<size_t>(kTerms) * (d.inter / 2);
-  w.h_terms = reinterpret_cast<uint8_t*>(take(P * hrow));
-  w.h_sf = reinterpret_cast<uint8_t*>(take(P * sfi));
-  w.pstride = static_cast<int>(P);
-  if (prefill) {
-    w.x_pterms = reinterpret_cast<uint8_t*>(take(P * term_ktile_row_bytes(d.hidden)));
-    w.x_psf = reinterpret_cast<uint8_t*>(take(P * sfh));
+  // the verify kernel's e2m1 term rows (calls of up to kTcPrefillMinTokens - 1 tokens)
+  const size_t mv = M < kTcPrefillMinTokens ? M : kTcPrefillMinTokens - 1;
+  w.x_terms = reinterpret_cast<uint8_t*>(take(mv * kTerms * (d.hidden / 2)));
+  w.x_sf = reinterpret_cast<uint8_t*>(take(mv * sfh));
+  w.h_terms = reinterpret_cast<uint8_t*>(take(mv * k * kTerms * (d.inter / 2)));
+  w.h_sf = reinterpret_cast<uint8_t*>(take(mv * k * sfi));
+  if (M >= kTcPrefillMinTokens) {   // the prefill kernel's bf16 row slices
+    w.pf_max_chunks = tc_pf_max_chunks(P, El);
+    w.pxb = reinterpret_cast<uint8_t*>(
+        take(static_cast<size_t>(w.pf_max_chunks) * (d.hidden / kTcPfK) * kTcPfBlk));
+    w.phb = reinterpret_cast<uint8_t*>(
+        take(static_cast<size_t>(w.pf_max_chunks) * (d.inter / kTcPfK) * kTcPfBlk));
+    w.pcf = reinterpret_cast<int32_t*>(take(static_cast<size_t>(w.pf_max_chunks) * kTcPfChunk * 4));
+    w.pcw = reinterpret_cast<float*>(take(static_cast<size_t>(w.pf_max_chunks) * kTcPfChunk * 4));
   }
   w.chunk_info = reinterpret_cast<int4*>(take(static_cast<size_t>(w.max_chunks) * 16));
   w.chunk_rows = reinterpret_cast<int32_t*>(take(static_cast<size_t>(w.max_chunks) * kChunkRowStride * 4));

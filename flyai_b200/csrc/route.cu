@@ -459,7 +459,7 @@ __device__ void route_plan_small(const int32_t* __restrict__ ids, int P, int e_b
       if (idx >= max_chunks) break;
       const int pos0 = off[e] + j * ct, nt = min(ct, c - j * ct);
       chunk_info[idx] = make_int4(e, pos0, nt, 0);
-      for (int i = 0; i < ct; ++i)
+      for (int i = 0; i < ct && i < kChunkRowStride; ++i)   // (prefill chunks read perm)
         chunk_rows[idx * kChunkRowStride + i] = i < nt ? perm_s[pos0 + i] / k : 0;
     }
   }

@@ -47,6 +47,28 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor(const void* smem_ptr, uint3
   return d;                                                      // no swizzle, base offset 0
 }
 
+// K-major with the 128-byte swizzle: row r of the operand is one 128-byte line
+// (64 16-bit elements of K) at r * 128, its 16-byte chunk q stored at chunk
+// position q ^ (r % 8), 8-row groups 1024 bytes apart (SBO); the leading offset
+// field is 1 (adjacent chunks).  The operand must start on a 1024-byte boundary;
+// the K = 16 step j of an MMA starts 32 * j bytes into the line (the hardware
+// applies the XOR on the address bits, so the start address moves by plain
+// offsets).  The same layout in global memory, copied with a bulk copy to a
+// 1024-aligned destination, keeps its swizzle.
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* smem_ptr) {
+  const uint32_t addr = smem_u32(smem_ptr);
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);   // start address   [0,14)
+  d |= 1ull << 16;                                     // leading offset  [16,30) = 16 B
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;         // stride offset   [32,46)
+  d |= 1ull << 46;                                     // descriptor version 1
+  d |= 2ull << 61;                                     // layout: 128-byte swizzle
+  return d;
+}
+__host__ __device__ __forceinline__ int sw128_offset(int r, int q) {
+  return r * 128 + ((q ^ (r & 7)) << 4);
+}
+
 // ---- instruction descriptor: block-scaled e2m1 x e2m1 (kind::mxf4) ------------
 // M = 128, N multiple of 8 in [16, 256], both operands K-major, ue8m0 scales per
 // 32 elements, dense K = 64 per instruction.  The scale-factor ids select the

@@ -23,7 +23,7 @@ from oracle import m25 as om25
 from oracle import v4 as ov4
 from oracle.topk import topk_row
 from tests.dsv3_util import M25_ULP_FRAC1, assert_close, expert_cache
-from tests.golden_util import assert_within_tolerance, bf16_tensor_to_f32, oracle_for_case
+from tests.golden_util import assert_within_tolerance, bf16_tensor_to_f32
 from tests.m25_util import dequant_expert
 from tests.v4_util import expert_np, shared_np
 

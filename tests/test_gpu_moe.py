@@ -1,8 +1,9 @@
 """GPU parity: the CUDA path (through the C ABI) against the CPU oracle and the
 reference fixtures.  Routing ids, logits and the permutation must match
-bit-exactly; expert outputs within rel-L2 5e-3 and max-abs 2e-2 x max|ref|, and
-element-wise within one bf16 step on 99.9 % of the elements and two everywhere
-(tests.golden_util.assert_within_tolerance)."""
+bit-exactly; expert outputs within rel-L2 5e-3 and max-abs 2e-2 x max|ref|,
+element-wise within one bf16 step on 99.9 % of the elements (99.7 % for the
+prefill kernel, whose tensor-core accumulation truncates) and within one bf16
+ulp at the output's peak everywhere (tests.golden_util.assert_within_tolerance)."""
 import glob
 import os
 
@@ -77,17 +78,46 @@ def test_gpt_oss_120b_verify_sizes(cfg1_layer, M):
     assert m["exact_frac"] > 0.9, m
 
 
+# Fraction of outputs within one bf16 step of the oracle for the prefill kernel.
+# Its tcgen05 kind::f16 MMAs add each K=16 group into the fp32 accumulator with a
+# truncation (round toward zero), 180 times over K = 2880, where the oracle rounds
+# the exact dot product once; a CPU model of that accumulation (exact group sums,
+# truncated adds) lands at the same fraction on these cases (0.9968 exact at M=72,
+# against 0.9997 for IEEE fp32 sums).
+PREFILL_ULP_FRAC1 = 0.997
+
+
+def test_prefill_matches_tensor_core_accumulation_model():
+    """The prefill kernel against the oracle with its projections accumulated as
+    the MMAs do (tests/tc_accum.py): the truncated K-group adds explain the
+    departures from the once-rounded oracle -- nearly every element agrees bit for
+    bit with the model, where about 0.3 % differ from the oracle."""
+    from tests.tc_accum import moe_forward_tc
+    layer = synth.make_gpt_oss_layer(**synth.GPT_OSS_20B, seed=21)
+    x = synth.make_tokens(72, 2880, seed=372)
+    ref = oracle_for_case(dict(layer=layer, x=x))
+    moe, out = run_layer(layer, x)
+    assert moe.read_error()[0] == 0
+    y = bf16_tensor_to_f32(out["y"])
+    y_tc = moe_forward_tc(x.float().numpy(), oracle_weights(layer), ref["ids"], ref["weights"])
+    m_tc = parity_metrics(y, y_tc)
+    m_or = parity_metrics(y, ref["y"])
+    print("vs model", m_tc, "vs oracle", m_or)
+    assert m_tc["exact_frac"] >= 0.999, m_tc
+    assert m_tc["exact_frac"] > m_or["exact_frac"]
+
+
 @pytest.mark.parametrize("M", [72, 256])
 def test_prefill_sizes_match_oracle(M):
-    """Batches of 65+ tokens take the prefill kernel (16-token chunks, activation
-    terms streamed with the weights); GPT-OSS-20B shape keeps the oracle fast."""
+    """Batches of 65+ tokens take the prefill kernel (128-pair chunks, weights
+    expanded to bf16 in shared memory); GPT-OSS-20B shape keeps the oracle fast."""
     layer = synth.make_gpt_oss_layer(**synth.GPT_OSS_20B, seed=21)
     x = synth.make_tokens(M, 2880, seed=300 + M)
     ref = oracle_for_case(dict(layer=layer, x=x))
     moe, out = run_layer(layer, x)
     assert moe.read_error()[0] == 0
     np.testing.assert_array_equal(out["ids"].cpu().numpy(), ref["ids"])
-    m = assert_within_tolerance(bf16_tensor_to_f32(out["y"]), ref["y"])
+    m = assert_within_tolerance(bf16_tensor_to_f32(out["y"]), ref["y"], ulp_frac1=PREFILL_ULP_FRAC1)
     assert m["exact_frac"] > 0.9, m
 
 
@@ -126,7 +156,7 @@ def test_config2_prefill_chunk_matches_oracle():
     hot_tok = np.nonzero((rids == hot).any(axis=1))[0]
     sub = sorted(set([0, 1, M // 2, M - 1] + hot_tok[[0, len(hot_tok) // 2, -1]].tolist()))
     ref = og.moe_forward(xc[sub], w, cpu.top_k)
-    m = assert_within_tolerance(bf16_tensor_to_f32(y)[sub], ref["y"])
+    m = assert_within_tolerance(bf16_tensor_to_f32(y)[sub], ref["y"], ulp_frac1=PREFILL_ULP_FRAC1)
     print("config 2 sample", sub, m)
 
 
