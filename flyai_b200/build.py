@@ -15,7 +15,7 @@ OUT_DIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(OUT_DIR, "libflyai_moe.so")
 SOURCES = ["abi.cu", "route.cu", "combine.cu", "tc_experts.cu", "tc_prefill.cu", "fp8_moe.cu", "nv4_moe.cu", "nv4_prefill.cu", "v4_moe.cu",
            "noalloc.cu"]
-HEADERS = ["common.cuh", "route.cuh", "torch_topk.cuh", "tcgen05.cuh", "terms.cuh", "tc_bank.cuh", "fp8_moe.cuh", "nv4.cuh", "v4.cuh"]
+HEADERS = ["common.cuh", "route.cuh", "route_dev.cuh", "torch_topk.cuh", "tcgen05.cuh", "terms.cuh", "tc_bank.cuh", "fp8_moe.cuh", "nv4.cuh", "v4.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -471,6 +471,13 @@ int flyai_moe_forward(const flyai_moe_desc* desc, int32_t M, const void* x,
     return launch_layer_experts(*desc, M, x, *w, y, fw.rows, fw, s);
   }
   const Workspace ws = carve_workspace(*desc, desc->max_tokens, workspace);
+  if (tc_fused_supported(*desc, M)) {   // verify size: the layer is one launch
+    const cudaEvent_t e0 = g_prof_start.load(), e1 = g_prof_stop.load();
+    if (e0 && e1 && cudaEventRecord(e0, s) != cudaSuccess) return FLYAI_ERR_CUDA;
+    FLYAI_TRY(launch_tc_forward(*desc, M, x, *w, y, topk_ids, topk_weights, ws, s));
+    if (e0 && e1 && cudaEventRecord(e1, s) != cudaSuccess) return FLYAI_ERR_CUDA;
+    return FLYAI_OK;
+  }
   FLYAI_TRY(launch_route(*desc, M, x, *w, nullptr, topk_ids, topk_weights, ws, s));
   const bool partial = (desc->expert_end - desc->expert_begin) != desc->num_experts;
   bool folded = false;

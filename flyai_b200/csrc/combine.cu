@@ -6,29 +6,9 @@
 // behind the expert kernel.
 #include "common.cuh"
 #include "route.cuh"
+#include "route_dev.cuh"
 
 namespace flyai {
-
-// The token's k slots in ascending expert id (ids of one token are distinct).
-__device__ __forceinline__ void slots_by_expert(const int32_t* __restrict__ ids, int m, int k,
-                                                int* order) {
-  int eid[kMaxTopK];
-  for (int s = 0; s < k; ++s) {
-    order[s] = s;
-    eid[s] = ids[m * k + s];
-  }
-  for (int i = 1; i < k; ++i) {
-    const int o = order[i], v = eid[i];
-    int j = i;
-    while (j > 0 && eid[j - 1] > v) {
-      eid[j] = eid[j - 1];
-      order[j] = order[j - 1];
-      --j;
-    }
-    eid[j] = v;
-    order[j] = o;
-  }
-}
 
 __device__ __forceinline__ void fold_rows(const uint16_t* __restrict__ rows, const int* order,
                                           int m, int k, int H, bool live, uint16_t* __restrict__ y) {

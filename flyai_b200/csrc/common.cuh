@@ -144,6 +144,22 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// L2 cache policy for data read once (weights streamed by the expert kernels):
+// its lines are the first candidates for eviction.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(pol));
+  return pol;
+}
+// bulk_g2s with an L2 cache policy (l2_policy_evict_first).
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;\n" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
 __device__ __forceinline__ int ld_acquire_gpu(const int32_t* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
@@ -220,6 +236,11 @@ __host__ __device__ inline int tc_pf_max_chunks(size_t P, size_t El) {
 constexpr int kTerms = 6;        // e2m1 terms an activation row is split into for kind::mxf4
 
 // ---- workspace layout -------------------------------------------------------
+// Words of the route ticket region (the first 512 bytes of the workspace in
+// every format; the FP8/NVFP4 layout uses words 0..65 only).
+constexpr int kTicketEp = 65;            // expert-parallel CTA count, failure word
+constexpr int kTicketGridBarrier = 67;   // fused layer's grid barrier: arrivals, generation
+
 // All regions 256-byte aligned, carved in this order from the caller's buffer.
 struct Workspace {
   float* logits;       // [M, E] fp32 holding bf16 values
@@ -233,20 +254,22 @@ struct Workspace {
   uint16_t* pair_out;  // [M*k, H] bf16 weighted expert outputs, flat pair order
   int32_t* err;        // [1] error bits set by kernels (kErr*)
   int32_t* dbg;        // [8] first failure details of the self-checking build
-  int32_t* route_ticket; // [1 + 64 + 2] at offset 0: tokens the fused route kernel
+  int32_t* route_ticket; // [1 + 64 + 2 + 2] at offset 0: tokens the fused route kernel
                          //     finished, per token its logit CTAs that finished, then
                          //     CTAs of the expert-parallel expert kernel that finished
-                         //     and whether one of them gave up on a wait; must be 0
-                         //     before first use, restored to 0 by every call
+                         //     and whether one of them gave up on a wait, then the fused
+                         //     layer's grid barrier (arrivals, generation); must be 0
+                         //     before first use, restored to 0 by every call (the
+                         //     generation word excepted: any value serves)
   int32_t* fold_ticket;  // [M * H/16] contributions per (token, 16-row output tile);
                          //     cleared by the route step of every call
   int32_t* n_chunks;   // [1] number of chunks (tc_chunk_tokens pairs each) over all non-empty experts
   int32_t* chunk_slot; // [max_chunks] active-list slot of each chunk
   int32_t* chunk_c0;   // [max_chunks] first token (within the expert) of each chunk
   uint8_t* x_terms;    // [M][H/32][kTerms][16] e2m1 terms of every token row (tensor-core path)
-  uint8_t* x_sf;       // [M][H/128][8][4] their e8m0 scales
+  uint8_t* x_sf;       // [M][H/128][8][16] their e8m0 scales (4 used bytes per 16)
   uint8_t* h_terms;    // [M*k][I/32][kTerms][16] terms of the SwiGLU rows, permuted order
-  uint8_t* h_sf;       // [M*k][I/128][8][4]
+  uint8_t* h_sf;       // [M*k][I/128][8][16]
   uint8_t* pxb;        // prefill only: [pf_max_chunks][H/64][kTcPfBlk] bf16 token rows by chunk
   uint8_t* phb;        // prefill only: [pf_max_chunks][I/64][kTcPfBlk] bf16 SwiGLU rows by chunk
   int32_t* pcf;        // prefill only: [pf_max_chunks][kTcPfChunk] flat pair index per chunk slot
@@ -274,7 +297,7 @@ inline Workspace carve_workspace(const flyai_moe_desc& d, int M, void* base) {
   // The route ticket sits at offset 0 whatever the descriptor, so a workspace
   // (or the no-allocation scratch array) reused with another descriptor still
   // finds it where the previous call restored it to zero.
-  w.route_ticket = reinterpret_cast<int32_t*>(take(4 * (1 + 64 + 2)));
+  w.route_ticket = reinterpret_cast<int32_t*>(take(4 * (kTicketGridBarrier + 2)));
   w.logits = reinterpret_cast<float*>(take(static_cast<size_t>(M) * E * 4));
   w.ids = reinterpret_cast<int32_t*>(take(P * 4));
   w.wts = reinterpret_cast<float*>(take(P * 4));
@@ -291,8 +314,9 @@ inline Workspace carve_workspace(const flyai_moe_desc& d, int M, void* base) {
   w.max_chunks = static_cast<int>(El + (P + kTcChunk - 1) / kTcChunk + 1);   // smallest chunk size
   w.chunk_slot = reinterpret_cast<int32_t*>(take(static_cast<size_t>(w.max_chunks) * 4));
   w.chunk_c0 = reinterpret_cast<int32_t*>(take(static_cast<size_t>(w.max_chunks) * 4));
-  const size_t sfh = static_cast<size_t>((d.hidden + 127) / 128) * 32;
-  const size_t sfi = static_cast<size_t>((d.inter + 127) / 128) * 32;
+  // term scale rows: per 128-K group 8 term slots of 16 bytes (terms.cuh)
+  const size_t sfh = static_cast<size_t>((d.hidden + 127) / 128) * 128;
+  const size_t sfi = static_cast<size_t>((d.inter + 127) / 128) * 128;
   // the verify kernel's e2m1 term rows (calls of up to kTcPrefillMinTokens - 1 tokens)
   const size_t mv = M < kTcPrefillMinTokens ? M : kTcPrefillMinTokens - 1;
   w.x_terms = reinterpret_cast<uint8_t*>(take(mv * kTerms * (d.hidden / 2)));

@@ -8,41 +8,11 @@
 #include "common.cuh"
 #include "route.cuh"
 #include "terms.cuh"
-#include "torch_topk.cuh"
+#include "route_dev.cuh"
 
 namespace flyai {
 
-// ---------------------------------------------------------------------------
-// 1) logits = round_bf16(x . W_r^T + b): one warp per (token, expert).
-// bf16*bf16 products are exact in fp32; summing them in fp64 makes the sum
-// exact to far below one bf16 ulp, so the single rounding reproduces the
-// reference CPU F.linear (which rounds once after fp32 accumulation) except
-// where that fp32 accumulation itself strays across a rounding boundary.
-// ---------------------------------------------------------------------------
-__device__ float logit_warp(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
-                            const uint16_t* __restrict__ br, int m, int e, int H) {
-  const int lane = threadIdx.x & 31;
-  const uint16_t* xr = x + static_cast<size_t>(m) * H;
-  const uint16_t* w = wr + static_cast<size_t>(e) * H;
-  double acc = 0.0;
-  for (int k0 = lane * 8; k0 < H; k0 += 256) {
-    const uint4 xv = *reinterpret_cast<const uint4*>(xr + k0);
-    const uint4 wv = *reinterpret_cast<const uint4*>(w + k0);
-    const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
-    const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float x0 = __uint_as_float(xs[i] << 16), x1 = __uint_as_float(xs[i] & 0xFFFF0000u);
-      const float w0 = __uint_as_float(ws[i] << 16), w1 = __uint_as_float(ws[i] & 0xFFFF0000u);
-      acc += static_cast<double>(__fmul_rn(x0, w0));
-      acc += static_cast<double>(__fmul_rn(x1, w1));
-    }
-  }
-  acc = warp_sum_f64(acc);
-  const double b = br ? static_cast<double>(bf16_bits_to_float(br[e])) : 0.0;
-  return bf16r(__double2float_rn(acc + b));
-}
-
+// 1) logits: logit_warp (route_dev.cuh), one warp per (token, expert).
 __global__ void __launch_bounds__(256) route_logits_kernel(const uint16_t* __restrict__ x,
                                                            const uint16_t* __restrict__ wr,
                                                            const uint16_t* __restrict__ br,
@@ -66,101 +36,7 @@ __global__ void __launch_bounds__(256) route_logits_kernel(const uint16_t* __res
   }
 }
 
-// ---------------------------------------------------------------------------
-// 2) torch CPU topk (sorted=True for GPT-OSS), via torch_topk.cuh's
-// restatement of libstdc++'s selection, run by one lane on a shared-memory copy
-// of the row when the fast path below cannot decide.
-// ---------------------------------------------------------------------------
-
-// One warp selects one token.  Fast path: when the k+1 largest values are
-// strictly decreasing (and nothing is NaN) the answer is unique -- the k
-// largest in descending order -- and is found with warp arg-max rounds.  Any
-// tie or NaN falls back to the serial libstdc++ restatement (torch_topk_serial).
-__device__ void select_softmax_token(const float* __restrict__ lr, KV* row, int m, int E, int k,
-                                     int32_t* __restrict__ ids, float* __restrict__ wts,
-                                     int32_t* __restrict__ ids_out, uint16_t* __restrict__ wts_out) {
-  const int lane = threadIdx.x & 31;
-  bool nan_seen = false;
-  for (int j = lane; j < E; j += 32) {
-    const float v = lr[j];
-    row[j] = KV{v, j};
-    nan_seen |= isnan(v);
-  }
-  __syncwarp();
-  const bool any_nan = __any_sync(0xffffffffu, nan_seen);
-
-  float top_v[kMaxTopK + 1];
-  int top_i[kMaxTopK + 1];
-  const int want = (k < E) ? k + 1 : k;
-  bool distinct = !any_nan;
-  if (distinct) {
-    // lanes own j = lane + 32*t; 'taken' bit t marks an element already chosen
-    uint32_t taken = 0;
-    for (int r = 0; r < want; ++r) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-      int bt = -1;
-      for (int t = 0, j = lane; j < E; ++t, j += 32) {
-        if (taken & (1u << t)) continue;
-        const float v = row[j].v;
-        if (bt < 0 || v > bv) {
-          bv = v;
-          bi = j;
-          bt = t;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-      top_v[r] = bv;
-      top_i[r] = bi;
-    }
-    for (int r = 1; r < want; ++r) distinct &= (top_v[r] < top_v[r - 1]);
-  }
-  if (!distinct) {
-    if (lane == 0) {
-      torch_topk_serial(row, E, k, true);
-      for (int r = 0; r < k; ++r) {
-        top_v[r] = row[r].v;
-        top_i[r] = row[r].i;
-      }
-    }
-    __syncwarp();
-    for (int r = 0; r < k; ++r) {
-      top_v[r] = __shfl_sync(0xffffffffu, top_v[r], 0);
-      top_i[r] = __shfl_sync(0xffffffffu, top_i[r], 0);
-    }
-  }
-  if (lane == 0) {
-    // softmax over the k selected bf16 logits in fp32, rounded to bf16
-    // (torch.nn.functional.softmax(top, dim=1, dtype=bfloat16))
-    float mx = top_v[0];
-    for (int r = 1; r < k; ++r) mx = fmaxf(mx, top_v[r]);
-    float ex[kMaxTopK];
-    float s = 0.f;
-    for (int r = 0; r < k; ++r) {
-      ex[r] = expf(__fsub_rn(top_v[r], mx));
-      s = __fadd_rn(s, ex[r]);
-    }
-    for (int r = 0; r < k; ++r) {
-      const float w = bf16r(__fdiv_rn(ex[r], s));
-      const size_t p = static_cast<size_t>(m) * k + r;
-      ids[p] = top_i[r];
-      wts[p] = w;
-      if (ids_out) ids_out[p] = top_i[r];
-      if (wts_out) wts_out[p] = float_to_bf16_bits(w);
-    }
-  }
-  __syncwarp();
-}
-
+// 2) top-k and gating weights: select_softmax_token (route_dev.cuh).
 __global__ void __launch_bounds__(256) route_select_softmax_kernel(
     const float* __restrict__ logits, int M, int E, int k, int32_t* __restrict__ ids,
     float* __restrict__ wts, int32_t* __restrict__ ids_out, uint16_t* __restrict__ wts_out) {
@@ -168,8 +44,10 @@ __global__ void __launch_bounds__(256) route_select_softmax_kernel(
   const int warp = threadIdx.x >> 5;
   const int m = blockIdx.x * 8 + warp;
   if (m >= M) return;
-  select_softmax_token(logits + static_cast<size_t>(m) * E, route_smem + warp * E, m, E, k, ids,
-                       wts, ids_out, wts_out);
+  // per warp: E (value, index) pairs, then the tie path's scratch
+  uint8_t* wsm = reinterpret_cast<uint8_t*>(route_smem) + warp * (E * sizeof(KV) + kTopkWarpScratch);
+  select_softmax_token(logits + static_cast<size_t>(m) * E, reinterpret_cast<KV*>(wsm), m, E, k, ids,
+                       wts, ids_out, wts_out, wsm + E * sizeof(KV));
 }
 
 // ---------------------------------------------------------------------------
@@ -518,7 +396,7 @@ __global__ void __launch_bounds__(kFusedRouteWarps * 32) route_fused_kernel(
   __threadfence();
   if (warp == 0)
     select_softmax_token(logits + static_cast<size_t>(m) * E, reinterpret_cast<KV*>(fused_smem), m,
-                         E, k, ids, wts, ids_out, wts_out);
+                         E, k, ids, wts, ids_out, wts_out, fused_smem + E * sizeof(KV));
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -544,7 +422,8 @@ int launch_route(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_
   const int El = d.expert_end - d.expert_begin;
   const bool tc = tc_supported(d);
   if (M > 0 && M <= kFusedRouteMaxTokens && M * k <= kSmallPlanMaxPairs && El <= 1024) {
-    const size_t smem = max(static_cast<size_t>(E) * sizeof(KV), small_plan_smem_bytes(M * k, El));
+    const size_t smem = max(static_cast<size_t>(E) * sizeof(KV) + kTopkWarpScratch,
+                            small_plan_smem_bytes(M * k, El));
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
@@ -578,7 +457,7 @@ int launch_route(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_
         static_cast<uint16_t*>(logits_out), tc && M < kTcPrefillMinTokens ? ws.x_terms : nullptr,
         tc && M < kTcPrefillMinTokens ? ws.x_sf : nullptr);   // prefill splits x after the plan
     note_launch();
-    const size_t smem = 8 * static_cast<size_t>(E) * sizeof(KV);
+    const size_t smem = 8 * (static_cast<size_t>(E) * sizeof(KV) + kTopkWarpScratch);
     route_select_softmax_kernel<<<(M + 7) / 8, 256, smem, stream>>>(
         ws.logits, M, E, k, ws.ids, ws.wts, ids_out, static_cast<uint16_t*>(wts_out));
     note_launch();

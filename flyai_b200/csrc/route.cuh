@@ -20,6 +20,13 @@ int launch_tc_experts(const flyai_moe_desc& d, int M, const void* x, bool x_spli
                       const flyai_moe_weights& w, uint16_t* pair_out, bool zero_pairs,
                       const Workspace& ws, cudaStream_t stream, void* y_fold = nullptr,
                       bool* folded = nullptr, const flyai_moe_ep_peers* ep = nullptr);
+// The whole verify-size layer in one launch (routing in the expert kernel's
+// prologue, the fold into y in its down epilogue): batches of 1..64 tokens with
+// at most 256 (token, slot) pairs on a GPU holding every expert.
+bool tc_fused_supported(const flyai_moe_desc& d, int M);
+int launch_tc_forward(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_weights& w,
+                      void* y, int32_t* ids_out, void* wts_out, const Workspace& ws,
+                      cudaStream_t stream);
 // Fold rows from this rank's mailbox once every rank's flag reached the epoch.
 int launch_combine_ep(const flyai_moe_desc& d, int M, const flyai_moe_ep_peers& ep, void* y,
                       const Workspace& ws, cudaStream_t stream);

@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "route.cuh"
+#include "route_dev.cuh"
 #include "tc_bank.cuh"
 #include "tcgen05.cuh"
 #include "terms.cuh"
@@ -137,7 +138,39 @@ struct TcParams {
   uint32_t* ep_flags[FLYAI_MOE_EP_MAX_RANKS];
   int32_t* ep_ticket;         // [0] CTAs that finished, [1] set when a wait gave up
                               // (workspace, self-resetting)
+  // fused verify layer (tc_moe_kernel<true>): routing in the prologue, fold in
+  // the down epilogue
+  struct Route {
+    const uint16_t* x;
+    const uint16_t* wr;
+    const uint16_t* br;
+    int M, E, k;
+    float* logits;                          // [M, E] workspace
+    int32_t* ids_ws;                        // [M*k] workspace copies of the routing
+    float* wts_ws;
+    int32_t* ids_out;                       // caller's top-k ids (int32) and weights (bf16)
+    uint16_t* wts_out;
+    int32_t* bar;                           // [2] grid barrier: arrivals, generation
+    int32_t* fold_cnt;                      // [M][down row tiles] pair rows stored per
+                                            // (token, 128-column slice of y)
+    uint16_t* y;
+    int clear_chunks;                       // chunk_done entries a call may use
+  } rt;
 };
+
+// Fused layer: at most this many (token, slot) pairs, so the plan fits in shared
+// memory next to the pipeline buffers.
+constexpr int kTcFusedMaxPairs = 256;
+// Plan kept in shared memory for the whole fused call: ids, weights, the
+// permutation, each token's slots in ascending expert id, chunk descriptors (a
+// chunk holds >= 1 pair, so <= P of them) and four words (chunk count, fold
+// mask, barrier status).
+constexpr size_t kTcPlanBytes = 4 * kTcFusedMaxPairs * 4 + kTcFusedMaxPairs * 16 + 16;
+// Per-warp top-k scratch of the fused prologue: E (value, index) pairs, E
+// logits, the tie path's working memory (16-byte multiple).
+__host__ __device__ inline size_t tc_topk_scratch(int E) {
+  return (static_cast<size_t>(E) * 12 + kTopkWarpScratch + 15) / 16 * 16;
+}
 
 // A bounded wait gave up: the error word gets kErrWaitTimeout and, under expert
 // parallelism, the call is marked failed so its peers do not fold partial rows.
@@ -172,16 +205,17 @@ __device__ __forceinline__ void tc_ep_signal(const TcParams& p) {
 // Shared memory: weight ring, two B buffers (kTcChunk term rows each), one
 // B-scale gather buffer, the SwiGLU hand-off and the mbarriers.
 struct TcSmem {
-  size_t b, b_bytes, sfb, hs, bars, total;
+  size_t b, b_bytes, sfb, hs, bars, plan, total;
 };
-__host__ __device__ inline TcSmem tc_smem_layout(int kmax, size_t tile_full) {
+__host__ __device__ inline TcSmem tc_smem_layout(int kmax, size_t tile_full, bool fused) {
   TcSmem m{};
   m.b = kTcStages * tile_full;
   m.b_bytes = (kTcChunk * term_row_bytes(kmax) + 32 + 127) / 128 * 128;
   m.sfb = m.b + 2 * m.b_bytes;
   m.hs = m.sfb + static_cast<size_t>((kmax + 127) / 128) * 512;
   m.bars = m.hs + 2 * kTcChunk * 64 * 4;
-  m.total = m.bars + (2 * kTcStages + 2 * kTcAcc + 8) * 8 + 16;
+  m.plan = m.bars + (2 * kTcStages + 2 * kTcAcc + 8) * 8 + 16;
+  m.total = m.plan + (fused ? kTcPlanBytes : 0);
   return m;
 }
 
@@ -190,14 +224,15 @@ __host__ __device__ inline TcSmem tc_smem_layout(int kmax, size_t tile_full) {
 // folds each token's k rows afterwards.
 __device__ __forceinline__ void tc_epilogue_down(const TcParams& p, const float (&val)[kTcChunk],
                                                  int nt, int pos0, int mt, int q, int lane,
-                                                 float bias_v) {
+                                                 float bias_v, const int32_t* perm,
+                                                 const float* wts) {
   const int o = mt * 128 + 32 * q + lane;
   if (o >= p.dn.L.R) return;
   for (int i = 0; i < nt; ++i) {
-    const int flat = p.perm[pos0 + i];
+    const int flat = perm[pos0 + i];
     float v = bf16r(val[i]);
     if (p.dn.bias) v = bf16r(__fadd_rn(v, bias_v));
-    v = bf16r(__fmul_rn(v, p.wts[flat]));
+    v = bf16r(__fmul_rn(v, wts[flat]));
     const uint16_t b = float_to_bf16_bits(v);
     const size_t at = static_cast<size_t>(flat) * p.hidden + o;
     if (p.ep_world == 0) {
@@ -208,11 +243,141 @@ __device__ __forceinline__ void tc_epilogue_down(const TcParams& p, const float 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fused verify layer: the prologue of tc_moe_kernel<true>
+// ---------------------------------------------------------------------------
+// A layer call at verify size is one launch.  Every CTA first takes units of
+// routing work -- the e2m1 split of one token row, or one expert's logits for
+// every token (router row held in registers, the same fp64 summation order as
+// logit_warp, so the logits equal the route kernel's bit for bit) -- then the
+// grid meets at one barrier (the grid is co-resident: a cooperative launch of
+// one CTA per SM).  After it every CTA reads all logits from L2, selects each
+// token's top-k (select_softmax_token: torch's order and bf16 softmax) and
+// builds the plan in its own shared memory; CTA 0 also writes the routing to
+// the workspace and the caller's outputs.  Identical inputs give identical
+// plans in every CTA, so no second grid-wide step is needed.
+
+// Sense-reversing grid barrier on two workspace words: the last CTA to arrive
+// restores the arrival count to zero and advances the generation the others
+// wait on (bounded, ~2 s).  One thread per CTA calls it.
+__device__ __forceinline__ bool tc_grid_barrier(int32_t* bar, int G) {
+  const int gen = ld_acquire_gpu(bar + 1);
+  __threadfence();
+  if (atomicAdd(bar, 1) == G - 1) {
+    // nothing touches the count again in this launch: a plain store, then the
+    // release of the generation (no round trip waited on)
+    asm volatile("st.relaxed.gpu.global.b32 [%0], %1;\n" ::"l"(bar), "r"(0) : "memory");
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;\n" ::"l"(bar + 1), "r"(1) : "memory");
+    return true;
+  }
+  const uint64_t t0 = global_ns();
+  while (true) {
+    for (int i = 0; i < 256; ++i)
+      if (ld_acquire_gpu(bar + 1) != gen) return true;
+    if (global_ns() - t0 > 2000000000ull) return false;
+    __nanosleep(256);
+  }
+}
+
+// Logits of expert e for every token: x . W_r[e] + b_r[e] rounded once to bf16
+// (bf16 products exact in fp32, summed in fp64 in logit_warp's order).  Warp w
+// takes tokens w, w + 8, ...; the router row stays in registers.
+__device__ __forceinline__ void tc_route_logits(const TcParams::Route& r, int e, int H) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kV = kTcMaxK / 256;
+  const uint16_t* w = r.wr + static_cast<size_t>(e) * H;
+  uint4 wv[kV];
+#pragma unroll
+  for (int i = 0; i < kV; ++i) {
+    const int k0 = lane * 8 + 256 * i;
+    wv[i] = k0 < H ? ldg_nc_v4(w + k0) : make_uint4(0, 0, 0, 0);
+  }
+  const double b = r.br ? static_cast<double>(bf16_bits_to_float(r.br[e])) : 0.0;
+  for (int m = warp; m < r.M; m += kTcThreads / 32) {
+    const uint16_t* xr = r.x + static_cast<size_t>(m) * H;
+    uint4 xv[kV];
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+      const int k0 = lane * 8 + 256 * i;
+      xv[i] = k0 < H ? *reinterpret_cast<const uint4*>(xr + k0) : make_uint4(0, 0, 0, 0);
+    }
+    double acc = 0.0;
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+      if (lane * 8 + 256 * i >= H) break;
+      const uint32_t xs[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+      const uint32_t ws[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float x0 = __uint_as_float(xs[j] << 16), x1 = __uint_as_float(xs[j] & 0xFFFF0000u);
+        const float w0 = __uint_as_float(ws[j] << 16), w1 = __uint_as_float(ws[j] & 0xFFFF0000u);
+        acc += static_cast<double>(__fmul_rn(x0, w0));
+        acc += static_cast<double>(__fmul_rn(x1, w1));
+      }
+    }
+    acc = warp_sum_f64(acc);
+    if (lane == 0) r.logits[static_cast<size_t>(m) * r.E + e] = bf16r(__double2float_rn(acc + b));
+  }
+}
+
+// The plan of route_plan_small (route.cu) built by the whole CTA in shared
+// memory, one thread per (token, slot) pair p (P <= kTcThreads): p's place in
+// the stable permutation is (pairs of lower experts) + (earlier pairs of its own
+// expert); a pair whose rank inside its expert is a multiple of kTcChunk opens a
+// chunk, numbered after the chunks of the lower experts.  Two passes over the
+// P ids in shared memory, no serial scan over the experts.  Returns the number
+// of chunks; every thread of the CTA must call.
+__device__ __forceinline__ int tc_fused_plan(const int32_t* ids_s, int P, int32_t* perm_s,
+                                             int32_t* rin_s, int4* cinfo_s) {
+  const int tid = threadIdx.x;
+  int e = 0, less = 0, rin = 0, cnt = 0;
+  if (tid < P) {
+    e = ids_s[tid];
+#pragma unroll 4
+    for (int q = 0; q < P; ++q) {
+      const int eq = ids_s[q];
+      less += eq < e;
+      rin += (eq == e) & (q < tid);
+      cnt += eq == e;
+    }
+    perm_s[less + rin] = tid;
+    rin_s[tid] = rin;
+  }
+  const bool opens = tid < P && rin % kTcChunk == 0;
+  const int nch = __syncthreads_count(opens);
+  if (opens) {
+    int before = 0;
+#pragma unroll 4
+    for (int q = 0; q < P; ++q) before += (ids_s[q] < e) & (rin_s[q] % kTcChunk == 0);
+    cinfo_s[before + rin / kTcChunk] = make_int4(e, less + rin, min(kTcChunk, cnt - rin), 0);
+  }
+  return nch;
+}
+
+// Column o of y for token m: the bf16 fold of the token's k weighted pair rows
+// in ascending expert id (combine_kernel's arithmetic); order_s holds each
+// token's slots in that order.  Called once the last of the token's k pair rows
+// of o's 128-column slice is stored.
+__device__ __forceinline__ void tc_fold_token(const TcParams& p, int m, int o,
+                                              const int32_t* order_s) {
+  const int k = p.rt.k, H = p.hidden;
+  uint16_t v[kMaxTopK];
+#pragma unroll
+  for (int s = 0; s < kMaxTopK; ++s)
+    if (s < k) v[s] = __ldcg(p.pair_out + (static_cast<size_t>(m) * k + order_s[m * k + s]) * H + o);
+  float a = 0.f;
+#pragma unroll
+  for (int s = 0; s < kMaxTopK; ++s)
+    if (s < k) a = bf16r(__fadd_rn(a, bf16_bits_to_float(v[s])));
+  p.rt.y[static_cast<size_t>(m) * H + o] = float_to_bf16_bits(a);
+}
+
+template <bool kFused>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ __align__(1024) uint8_t tsm[];
   constexpr int S = kTcStages;
   const size_t tile_full = p.gu.L.tile_full;
-  const TcSmem m = tc_smem_layout(p.kmax, tile_full);
+  const TcSmem m = tc_smem_layout(p.kmax, tile_full, kFused);
   uint8_t* ring = tsm;
   uint8_t* bsm = tsm + m.b;            // buffer j at bsm + j * m.b_bytes
   uint8_t* sfbsm = tsm + m.sfb;
@@ -255,14 +420,98 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = *tmem_slot;
-  pdl_wait();   // routing plan, x terms and cleared counters are visible
+  pdl_wait();   // routing plan, x terms and cleared counters are visible (x alone when fused)
+  // the plan: workspace arrays written by the route kernel, or (fused) this
+  // CTA's own copy in shared memory
+  const int4* cinfo = p.chunk_info;
+  const int32_t* perm = p.perm;
+  const float* wts = p.wts;
+  const int32_t* plan_order = nullptr;
+  int32_t* plan_words = nullptr;   // fused: [1] fold mask, [2] barrier passed
+  long long nch;
+  if constexpr (kFused) {
+    const TcParams::Route& r = p.rt;
+    const int H = p.hidden, P = r.M * r.k;
+    uint8_t* pl = tsm + m.plan;
+    int32_t* ids_s = reinterpret_cast<int32_t*>(pl);
+    float* wts_s = reinterpret_cast<float*>(pl + kTcFusedMaxPairs * 4);
+    int32_t* perm_s = reinterpret_cast<int32_t*>(pl + 2 * kTcFusedMaxPairs * 4);
+    int32_t* order_s = reinterpret_cast<int32_t*>(pl + 3 * kTcFusedMaxPairs * 4);
+    int4* cinfo_s = reinterpret_cast<int4*>(pl + 4 * kTcFusedMaxPairs * 4);
+    plan_words = reinterpret_cast<int32_t*>(pl + 4 * kTcFusedMaxPairs * 4 + kTcFusedMaxPairs * 16);
+    // units: token rows to e2m1 terms, then one expert's logits each
+    for (int u = blockIdx.x; u < r.M + r.E; u += gridDim.x) {
+      if (u < r.M)
+        decompose_rows(r.x, H, H, u, 1, const_cast<uint8_t*>(p.gu.act_terms) + u * term_row_bytes(H),
+                       const_cast<uint8_t*>(p.gu.act_sf) + u * term_sf_row_bytes(H));
+      else
+        tc_route_logits(r, u - r.M, H);
+    }
+    if (blockIdx.x == 0) {   // counters the call's items advance start at zero
+      for (int i = threadIdx.x; i < r.clear_chunks; i += kTcThreads) p.chunk_done[i] = 0;
+      for (int i = threadIdx.x; i < r.M * p.dn.L.MT; i += kTcThreads) r.fold_cnt[i] = 0;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) plan_words[2] = tc_grid_barrier(r.bar, gridDim.x);
+    __syncthreads();
+    if (!plan_words[2]) {   // the grid never met: nothing of this call is valid
+      if (threadIdx.x == 0) atomicOr(p.err, kErrWaitTimeout);
+      if (warp == 1) tc::tmem_dealloc(tbase, 512);
+      return;
+    }
+    // every token's top-k from the logits in L2 (scratch: the weight ring; per
+    // warp E (value, index) pairs, E logits and the tie path's scratch)
+    uint8_t* wsc = tsm + static_cast<size_t>(warp) * tc_topk_scratch(r.E);
+    KV* kv = reinterpret_cast<KV*>(wsc);
+    float* lrow = reinterpret_cast<float*>(wsc + r.E * sizeof(KV));
+    for (int mm = warp; mm < r.M; mm += kTcThreads / 32) {
+      for (int j = lane; j < r.E; j += 32) lrow[j] = __ldcg(r.logits + static_cast<size_t>(mm) * r.E + j);
+      __syncwarp();
+      select_softmax_token(lrow, kv, mm, r.E, r.k, ids_s, wts_s, nullptr, nullptr,
+                           wsc + r.E * (sizeof(KV) + 4));
+      __syncwarp();
+    }
+    __syncthreads();
+    const int n_plan = tc_fused_plan(
+        ids_s, P, perm_s,
+        reinterpret_cast<int32_t*>(tsm + static_cast<size_t>(kTcThreads / 32) * tc_topk_scratch(r.E)),
+        cinfo_s);
+    if (threadIdx.x < P) {   // slot order of each token by expert id (ids of a token differ)
+      const int tok = threadIdx.x / r.k, e = ids_s[threadIdx.x];
+      int rank = 0;
+      for (int s2 = 0; s2 < r.k; ++s2) rank += ids_s[tok * r.k + s2] < e;
+      order_s[tok * r.k + rank] = threadIdx.x - tok * r.k;
+    }
+    if (blockIdx.x == 0) {
+      for (int i = threadIdx.x; i < P; i += kTcThreads) {
+        r.ids_ws[i] = ids_s[i];
+        r.wts_ws[i] = wts_s[i];
+        if (r.ids_out) r.ids_out[i] = ids_s[i];
+        if (r.wts_out) r.wts_out[i] = float_to_bf16_bits(wts_s[i]);
+      }
+    }
+    // the ring's generic-proxy scratch writes come before its bulk-copy writes,
+    // and other CTAs' token terms (generic stores before the barrier) before the
+    // bulk copies that read them
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    fence_proxy_async_global();
+    __syncthreads();
+    cinfo = cinfo_s;
+    perm = perm_s;
+    wts = wts_s;
+    plan_order = order_s;
+    nch = n_plan;
+  } else {
+    nch = *p.n_chunks;
+  }
   pdl_launch_dependents();
   const int mtg = p.gu.L.MT, mtd = p.dn.L.MT;
   TcCursor cur;
   {
-    const long long nch = *p.n_chunks, G = gridDim.x, b = blockIdx.x;
-    const long long n_gu = nch * mtg, n_dn = nch * mtd;
-    const long long g0 = n_gu * b / G, d0 = n_dn * b / G;
+    // item counts stay far below 2^31 / gridDim (<= 256 chunks x 48 tiles)
+    const unsigned G = gridDim.x, b = blockIdx.x;
+    const unsigned n_gu = static_cast<unsigned>(nch) * mtg, n_dn = static_cast<unsigned>(nch) * mtd;
+    const unsigned g0 = n_gu * b / G, d0 = n_dn * b / G;
     cur.start(g0, n_gu * (b + 1) / G - g0, d0, n_dn * (b + 1) / G - d0, mtg, mtd);
   }
   if (!cur.valid()) {   // nothing for this CTA
@@ -270,16 +519,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
     if (threadIdx.x == 0 && p.ep_world) tc_ep_signal(p);
     return;
   }
+  // token row of slot i of a gate/up chunk
+  auto chunk_row = [&](int chunk, int pos0, int i) -> int {
+    if constexpr (kFused) return perm[pos0 + i] / p.rt.k;
+    else return __ldg(&p.chunk_rows[chunk * kChunkRowStride + i]);
+  };
 
   if (warp == 0) {
     // ---------------- producer: weight tiles into the ring ----------------
+    // Weight tiles are read once: their copies carry an evict-first L2 policy,
+    // so they recycle each other's L2 lines instead of evicting (and writing
+    // back) whatever else the L2 holds.
     bool ok = true;
     uint32_t li = 0;
+    const uint64_t stream_policy = l2_policy_evict_first();
     for (; cur.valid(); cur.next()) {
       if (lane == 0 && ok) {
         const TcItem t = cur.t;
         const TcProj& P = t.gu ? p.gu : p.dn;
-        const int e = __ldg(&p.chunk_info[t.chunk].x);
+        const int e = cinfo[t.chunk].x;
         const int rows_t = tc_rows(P.L, t.mt);
         const uint8_t* src =
             P.bank + static_cast<size_t>(e) * P.L.expert_bytes + static_cast<size_t>(t.mt) * P.L.mtile_full;
@@ -291,7 +549,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
           }
           const uint32_t bytes = static_cast<uint32_t>(tc_tile_bytes(rows_t, tc_kt_len(P.L, kt)));
           mbar_expect_tx(&full[s], bytes);
-          bulk_g2s(ring + s * tile_full, src, bytes, &full[s]);
+          bulk_g2s_hint(ring + s * tile_full, src, bytes, &full[s], stream_policy);
           src += bytes;
         }
       }
@@ -319,7 +577,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
     TcItem prev{-1, -1, -1};
     const uint32_t idesc[2] = {tc::idesc_mxf4(kTcN, 0, 0), tc::idesc_mxf4(kTcN, 2, 2)};
     const uint64_t cp_ring = tc::smem_desc_kmajor(ring, 0, 128);
-    const uint64_t cp_sfb = tc::smem_desc_kmajor(sfbsm, 0, 128);
+    // B scales: token-major rows (srb bytes each), one 8-row core matrix per token
+    const uint64_t cp_sfb_gu = tc::smem_desc_kmajor(sfbsm, 0, static_cast<uint32_t>(term_sf_row_bytes(p.gu.L.K)));
+    const uint64_t cp_sfb_dn = tc::smem_desc_kmajor(sfbsm, 0, static_cast<uint32_t>(term_sf_row_bytes(p.dn.L.K)));
     const uint64_t b_gu = tc::smem_desc_kmajor(bsm, kTcBlockBytes, term_row_bytes(p.gu.L.K));
     const uint64_t b_dn = tc::smem_desc_kmajor(bsm, kTcBlockBytes, term_row_bytes(p.dn.L.K));
     const uint32_t b_step = static_cast<uint32_t>(m.b_bytes >> 4);
@@ -340,7 +600,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
         if (!odd) {
           const int ng = (P.L.K + 127) / 128;
           if (elect_one()) {
-            for (int g = 0; g < ng; ++g) tc::copy_sf_chunk_desc(sfb_col + 4 * g, cp_sfb + 32 * g);
+            const uint64_t cp_sfb = t.gu ? cp_sfb_gu : cp_sfb_dn;
+            for (int g = 0; g < ng; ++g)
+              tc::copy_sf_chunk_desc(sfb_col + 4 * g, cp_sfb + (kTermSfGroupBytes >> 4) * g);
             tc::commit_to(sfb_done);
           }
           __syncwarp();
@@ -417,7 +679,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
     bool ok = true;
     uint32_t item_no = 0;
     int chunk_items = 0;
-    int4 ci = __ldg(&p.chunk_info[cur.t.chunk]);   // chunk of the current item
+    int4 ci = cinfo[cur.t.chunk];   // chunk of the current item
     for (; cur.valid(); cur.next(), ++item_no) {
       const TcItem t = cur.t;
       const TcProj& P = t.gu ? p.gu : p.dn;
@@ -431,7 +693,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
       if (!same_next) {
         TcCursor nx = cur;
         nx.next();
-        if (nx.valid()) ci_next = __ldg(&p.chunk_info[nx.t.chunk]);
+        if (nx.valid()) ci_next = cinfo[nx.t.chunk];
       }
       ++chunk_items;
       const uint32_t buf = item_no % kTcAcc, use = item_no / kTcAcc;
@@ -524,7 +786,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
           }
         }
       } else {
-        tc_epilogue_down(p, val, ok ? nt : 0, pos0, t.mt, q, lane, bias_v);
+        tc_epilogue_down(p, val, ok ? nt : 0, pos0, t.mt, q, lane, bias_v, perm, wts);
+        if constexpr (kFused) {
+          // a token whose k pair rows of this 128-column slice are now all stored
+          // is folded into y here (the item's tokens are distinct)
+          __threadfence();
+          named_barrier_sync(1, 128);
+          if (et < kTcChunk) {
+            bool last = false;
+            if (et < nt) {
+              const int m = perm[pos0 + et] / p.rt.k;
+              last = atomicAdd(&p.rt.fold_cnt[m * mtd + t.mt], 1) == p.rt.k - 1;
+            }
+            const uint32_t mask = __ballot_sync(0xfu, last);
+            if (et == 0) plan_words[1] = static_cast<int>(mask);
+          }
+          named_barrier_sync(1, 128);
+          const uint32_t mask = static_cast<uint32_t>(plan_words[1]);
+          if (mask) {
+            __threadfence();
+            const int o = t.mt * 128 + 32 * q + lane;
+            for (int i = 0; i < kTcChunk; ++i)
+              if (((mask >> i) & 1u) && o < p.hidden) tc_fold_token(p, perm[pos0 + i] / p.rt.k, o, plan_order);
+          }
+        }
       }
       if (!same_next) chunk_items = 0;
       ci = ci_next;
@@ -537,9 +822,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
     // ---------------- B stager: activation terms of each chunk ----------------
     // Token i's whole term row lands at B + i*trb by one bulk copy; the MMA
     // reads it as core matrices of 8 term slots (slots past kTerms overlap the
-    // next block and feed columns nobody reads).  Scales are gathered into the
-    // tcgen05.cp chunk layout: row n = token*8 + slot at (n%32)*16 + (n/32)*4.
-    // Two B buffers let the next chunk's terms arrive while this one computes.
+    // next block and feed columns nobody reads).  Token i's scale row lands at
+    // i * srb by one more bulk copy: the 8 term slots of one 128-K group are one
+    // 8-row core matrix of tcgen05.cp's 32x128b chunk, and the copy's descriptor
+    // strides srb from token to token (row n = token*8 + slot).  Two B buffers
+    // let the next chunk's terms arrive while this one computes.
     bool ok = true;
     uint32_t bc = 0;
     TcItem prev{-1, -1, -1};
@@ -548,7 +835,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
       if (tc_same_b(t, prev)) continue;
       prev = t;
       const TcProj& P = t.gu ? p.gu : p.dn;
-      const int4 ci = __ldg(&p.chunk_info[t.chunk]);
+      const int4 ci = cinfo[t.chunk];
       const int nt = ci.z;
       const uint32_t j = bc & 1;
       if (lane == 0) {
@@ -564,27 +851,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
       if (!ok) break;
       const size_t trb = term_row_bytes(P.L.K), srb = term_sf_row_bytes(P.L.K);
       uint8_t* bj = bsm + j * m.b_bytes;
-      if (lane == 0) mbar_expect_tx_only(&b_full[j], static_cast<uint32_t>(nt * trb));
+      if (lane == 0) mbar_expect_tx_only(&b_full[j], static_cast<uint32_t>(nt * (trb + srb)));
       __syncwarp();
       if (lane < nt) {
-        const int row = t.gu ? __ldg(&p.chunk_rows[t.chunk * kChunkRowStride + lane]) : ci.y + lane;
+        const int row = t.gu ? chunk_row(t.chunk, ci.y, lane) : ci.y + lane;
         bulk_g2s(bj + lane * trb, P.act_terms + static_cast<size_t>(row) * trb,
                  static_cast<uint32_t>(trb), &b_full[j]);
       }
-      const int ng = (P.L.K + 127) / 128;
-      for (int u = lane; u < nt * ng * 2; u += 32) {
-        const int i = u / (ng * 2), rem = u % (ng * 2), g = rem >> 1, half = rem & 1;
-        const int row = t.gu ? __ldg(&p.chunk_rows[t.chunk * kChunkRowStride + i]) : ci.y + i;
-        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(P.act_sf + static_cast<size_t>(row) * srb +
-                                                               g * 32 + half * 16));
-        uint32_t* dst = reinterpret_cast<uint32_t*>(sfbsm + static_cast<size_t>(g) * 512 +
-                                                    (i * 8 + half * 4) * 16);
-        dst[0] = v.x;
-        dst[4] = v.y;
-        dst[8] = v.z;
-        dst[12] = v.w;
+      // scales: token i's whole scale row at i * srb; the tcgen05.cp descriptor
+      // of group g strides srb between the tokens' 8-row core matrices
+      if (lane >= 16 && lane - 16 < nt) {
+        const int i = lane - 16;
+        const int row = t.gu ? chunk_row(t.chunk, ci.y, i) : ci.y + i;
+        bulk_g2s(sfbsm + static_cast<size_t>(i) * srb, P.act_sf + static_cast<size_t>(row) * srb,
+                 static_cast<uint32_t>(srb), &b_full[j]);
       }
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&b_full[j]);
       ++bc;
@@ -625,6 +906,28 @@ static cudaError_t tc_launch_pdl(Kern kernel, int grid, int block, size_t smem, 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// The persistent expert kernel: one CTA per SM whose items wait on other CTAs
+// (a chunk's down tiles on its gate/up tiles; the fused layer's grid barrier),
+// so the grid must be co-resident.  A cooperative launch guarantees that or
+// fails with an error instead of leaving CTAs waiting for SMs held by others.
+static cudaError_t tc_launch_persistent(const TcParams& prm, bool fused, int grid, size_t smem,
+                                        cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return fused ? cudaLaunchKernelEx(&cfg, tc_moe_kernel<true>, prm)
+               : cudaLaunchKernelEx(&cfg, tc_moe_kernel<false>, prm);
 }
 
 int launch_tc_experts(const flyai_moe_desc& d, int M, const void* x, bool x_split,
@@ -689,18 +992,77 @@ int launch_tc_experts(const flyai_moe_desc& d, int M, const void* x, bool x_spli
       prm.ep_flags[r] = reinterpret_cast<uint32_t*>(mb);
       prm.ep_rows[r] = reinterpret_cast<uint16_t*>(mb + kEpFlagBytes + (ep->epoch & 1) * rows_bytes);
     }
-    prm.ep_ticket = ws.route_ticket + 65;
+    prm.ep_ticket = ws.route_ticket + kTicketEp;
   }
 
-  const size_t smem = tc_smem_layout(prm.kmax, prm.gu.L.tile_full).total;
+  const size_t smem = tc_smem_layout(prm.kmax, prm.gu.L.tile_full, false).total;
   if (smem > static_cast<size_t>(max_smem) || prm.kmax > kTcMaxK) return FLYAI_ERR_UNSUPPORTED;
-  if (cudaFuncSetAttribute(tc_moe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(tc_moe_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
     return FLYAI_ERR_CUDA;
-  if (tc_launch_pdl(tc_moe_kernel, sms, kTcThreads, smem, stream, prm) != cudaSuccess)
-    return FLYAI_ERR_CUDA;
+  if (tc_launch_persistent(prm, false, sms, smem, stream) != cudaSuccess) return FLYAI_ERR_CUDA;
   note_launch();
   (void)y_fold;   // the caller folds pair rows into y with launch_combine
+  return FLYAI_OK;
+}
+
+bool tc_fused_supported(const flyai_moe_desc& d, int M) {
+  return M >= 1 && M < kTcPrefillMinTokens && M * d.top_k <= kTcFusedMaxPairs &&
+         d.expert_begin == 0 && d.expert_end == d.num_experts;
+}
+
+int launch_tc_forward(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_weights& w,
+                      void* y, int32_t* ids_out, void* wts_out, const Workspace& ws,
+                      cudaStream_t stream) {
+  int dev = 0, sms = 0, max_smem = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  TcParams prm{};
+  prm.gu = TcProj{static_cast<const uint8_t*>(w.w13), tc_layout(d, FLYAI_PROJ_W13),
+                  static_cast<const float*>(w.w13_bias), ws.x_terms, ws.x_sf};
+  prm.dn = TcProj{static_cast<const uint8_t*>(w.w2), tc_layout(d, FLYAI_PROJ_W2),
+                  static_cast<const float*>(w.w2_bias), ws.h_terms, ws.h_sf};
+  prm.chunk_done = ws.chunk_done;
+  prm.h_terms = ws.h_terms;
+  prm.h_sf = ws.h_sf;
+  prm.pair_out = ws.pair_out;
+  prm.hidden = d.hidden;
+  prm.inter = d.inter;
+  prm.kmax = d.hidden > d.inter ? d.hidden : d.inter;
+  prm.limit = d.swiglu_limit;
+  prm.alpha = d.swiglu_alpha;
+  prm.err = ws.err;
+  TcParams::Route& r = prm.rt;
+  r.x = static_cast<const uint16_t*>(x);
+  r.wr = static_cast<const uint16_t*>(w.router_w);
+  r.br = static_cast<const uint16_t*>(w.router_b);
+  r.M = M;
+  r.E = d.num_experts;
+  r.k = d.top_k;
+  r.logits = ws.logits;
+  r.ids_ws = ws.ids;
+  r.wts_ws = ws.wts;
+  r.ids_out = ids_out;
+  r.wts_out = static_cast<uint16_t*>(wts_out);
+  r.bar = ws.route_ticket + kTicketGridBarrier;
+  r.fold_cnt = ws.fold_ticket;
+  r.y = static_cast<uint16_t*>(y);
+  r.clear_chunks = M * d.top_k < ws.max_chunks ? M * d.top_k : ws.max_chunks;
+
+  const size_t smem = tc_smem_layout(prm.kmax, prm.gu.L.tile_full, true).total;
+  // prologue scratch in the weight ring: per warp E (value, index) pairs and E
+  // logits, then the plan's counters
+  const size_t scratch = static_cast<size_t>(kTcThreads / 32) * tc_topk_scratch(d.num_experts) +
+                         (static_cast<size_t>(M) * d.top_k + 3 * d.num_experts + 2) * 4;
+  if (smem > static_cast<size_t>(max_smem) || prm.kmax > kTcMaxK ||
+      scratch > kTcStages * prm.gu.L.tile_full)
+    return FLYAI_ERR_UNSUPPORTED;
+  if (cudaFuncSetAttribute(tc_moe_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return FLYAI_ERR_CUDA;
+  if (tc_launch_persistent(prm, true, sms, smem, stream) != cudaSuccess) return FLYAI_ERR_CUDA;
+  note_launch();
   return FLYAI_OK;
 }
 

@@ -41,25 +41,29 @@ __device__ __forceinline__ float2 e2m1x2_to_f32x2(uint32_t byte) {
 //          whole K are one contiguous run that a bulk copy moves as-is; the MMA
 //          reads it as 8-row core matrices (terms 0..7, slots past kTerms see the
 //          next block and are ignored) with a 96-byte K stride;
-//   scales [K/128 groups of 4 blocks][8 term slots][4 bytes] -- e8m0 of
-//          (term, block); slot t holds the 4 blocks of one 128-element group,
-//          the word the tensor-memory scale layout wants per (row, group).
+//   scales [K/128 groups of 4 blocks][8 term slots][16 bytes] -- e8m0 of
+//          (term, block) in the first 4 bytes of slot t (the 4 blocks of one
+//          128-element group: the word the tensor-memory scale layout wants per
+//          (row, group)); the other 12 bytes are padding.  A token's 128 bytes
+//          of one group are 8 consecutive rows of tcgen05.cp's 32x128b scale
+//          chunk, so a chunk's B scales are assembled by 128-byte bulk copies.
 constexpr int kTermSlots = 8;
 static_assert(kTerms <= kTermSlots, "terms must fit the 8-row core matrix of a token");
 __host__ __device__ __forceinline__ size_t term_row_bytes(int K) {
   return static_cast<size_t>(K / 32) * kTerms * 16;
 }
+constexpr int kTermSfGroupBytes = kTermSlots * 16;   // one token's scales of one 128-K group
 __host__ __device__ __forceinline__ size_t term_sf_row_bytes(int K) {
-  return static_cast<size_t>((K + 127) / 128) * kTermSlots * 4;
+  return static_cast<size_t>((K + 127) / 128) * kTermSfGroupBytes;
 }
 __host__ __device__ __forceinline__ size_t term_sf_offset(int block, int term) {
-  return static_cast<size_t>(block / 4) * kTermSlots * 4 + term * 4 + block % 4;
+  return static_cast<size_t>(block / 4) * kTermSfGroupBytes + term * 16 + block % 4;
 }
 
 // One 32-element block held as 8 consecutive values by each of 4 adjacent
 // lanes (quarter = lane & 3); all 32 lanes of the warp must call (shuffles).
 // With store, writes this lane's 4 packed bytes of term t at tb + t*16 +
-// quarter*4 and, from quarter 0, the block's e8m0 scale of term t at sb + t*4
+// quarter*4 and, from quarter 0, the block's e8m0 scale of term t at sb + t*16
 // (tb, sb: the block's place in the row layouts above).
 __device__ __forceinline__ void decompose_block(float (&v)[8], int quarter, uint8_t* tb,
                                                 uint8_t* sb, bool store) {
@@ -90,7 +94,7 @@ __device__ __forceinline__ void decompose_block(float (&v)[8], int quarter, uint
     }
     if (store) {
       *reinterpret_cast<uint32_t*>(tb + t * 16 + quarter * 4) = word;
-      if (quarter == 0) sb[t * 4] = static_cast<uint8_t>(e + 127);
+      if (quarter == 0) sb[t * 16] = static_cast<uint8_t>(e + 127);
     }
   }
 }
@@ -130,7 +134,7 @@ __device__ __forceinline__ void decompose_rows(const uint16_t* src, int ld, int 
   for (int i = threadIdx.x; i < nrows * groups * kTermSlots * 4; i += blockDim.x) {
     const int r = i / (groups * kTermSlots * 4), rem = i % (groups * kTermSlots * 4);
     const int g = rem / (kTermSlots * 4), t = (rem / 4) % kTermSlots, b = g * 4 + rem % 4;
-    if (t >= kTerms || b >= blocks) sf[r * srb + rem] = 127;
+    if (t >= kTerms || b >= blocks) sf[r * srb + g * kTermSfGroupBytes + t * 16 + b % 4] = 127;
   }
 }
 
