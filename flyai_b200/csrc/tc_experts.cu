@@ -98,17 +98,17 @@ int launch_tc_pack(const flyai_moe_desc& d, int proj, const void* blocks, const 
 // The fused expert kernel
 // ---------------------------------------------------------------------------
 // Work items: (chunk, 128-row tile) of the gate/up projection and of the down
-// projection.  Each CTA takes one contiguous share of the gate/up items and the
-// matching share of the down items, in that order, so the down tiles of a chunk
-// land on about the CTAs that computed its gate/up tiles.  A chunk is up to
+// projection, dealt to the CTAs round-robin in runs of kTcRun, gate/up first.  A chunk is up to
 // kTcChunk tokens of one expert; its down tiles wait until all of its gate/up
 // tiles (on any CTA) have written the SwiGLU rows, counted in chunk_done.
 // Gate/up items never wait on anything and come first in every CTA, so the
-// waits resolve.
+// waits resolve; a chunk's gate/up tiles are dealt within one or two rounds,
+// so they are long done when its down tiles come up.
 constexpr int kTcN = kTcChunk * kTermSlots;                // 32: MMA N, column token*8 + term
 constexpr int kTcAcc = 4;                                  // accumulator buffers
 constexpr int kTcAccCols = 2 * kTcN;                       // even / odd K-tile halves
 constexpr int kTcStages = 4;
+constexpr int kTcRun = 3;                                  // items per dealt run (TcRunCursor)
 constexpr int kTcSfaCol = kTcAcc * kTcAccCols;             // A scales: 16 columns per ring stage
 constexpr int kTcSfbCol = kTcSfaCol + 16 * kTcStages;      // B scales: 2 buffers x 4 per K group
 static_assert(kTcSfbCol + 2 * 4 * (kTcMaxK / 128) <= 512, "tensor memory budget");
@@ -506,14 +506,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
   }
   pdl_launch_dependents();
   const int mtg = p.gu.L.MT, mtd = p.dn.L.MT;
-  TcCursor cur;
-  {
-    // item counts stay far below 2^31 / gridDim (<= 256 chunks x 48 tiles)
-    const unsigned G = gridDim.x, b = blockIdx.x;
-    const unsigned n_gu = static_cast<unsigned>(nch) * mtg, n_dn = static_cast<unsigned>(nch) * mtd;
-    const unsigned g0 = n_gu * b / G, d0 = n_dn * b / G;
-    cur.start(g0, n_gu * (b + 1) / G - g0, d0, n_dn * (b + 1) / G - d0, mtg, mtd);
-  }
+  // Runs of kTcRun items dealt round-robin, gate/up then down (TcRunCursor).
+  TcRunCursor<kTcRun> cur;
+  cur.start(blockIdx.x, gridDim.x, nch, mtg, mtd);
   if (!cur.valid()) {   // nothing for this CTA
     if (warp == 1) tc::tmem_dealloc(tbase, 512);
     if (threadIdx.x == 0 && p.ep_world) tc_ep_signal(p);
@@ -691,7 +686,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
       const bool same_next = cur.next_same_b();
       int4 ci_next = ci;
       if (!same_next) {
-        TcCursor nx = cur;
+        TcRunCursor<kTcRun> nx = cur;
         nx.next();
         if (nx.valid()) ci_next = cinfo[nx.t.chunk];
       }
