@@ -958,6 +958,9 @@ __global__ void __launch_bounds__(kF8Threads, 1) f8_moe_kernel(const __grid_cons
 
   if (warp == 0) {
     // ---------------- producer ----------------
+    // weights are read once: evict-first L2 policy (they recycle each other's
+    // lines instead of evicting what else the L2 holds)
+    const uint64_t wpol = l2_policy_evict_first();
     bool ok = true;
     uint32_t ks = 0;
     for (; cur.valid(); cur.next()) {
@@ -981,7 +984,7 @@ __global__ void __launch_bounds__(kF8Threads, 1) f8_moe_kernel(const __grid_cons
               break;
             }
             mbar_expect_tx(&full[s], abytes + kF8BBytes);
-            bulk_g2s(ring + s * kF8Stage, a + static_cast<size_t>(kb) * abytes, abytes, &full[s]);
+            bulk_g2s_hint(ring + s * kF8Stage, a + static_cast<size_t>(kb) * abytes, abytes, &full[s], wpol);
           }
           if (!wait_counter_geq(&p.chunk_done[t.chunk], NI)) ok = false;
           fence_proxy_async_global();
@@ -998,7 +1001,7 @@ __global__ void __launch_bounds__(kF8Threads, 1) f8_moe_kernel(const __grid_cons
             break;
           }
           mbar_expect_tx(&full[s], abytes + kF8BBytes);
-          bulk_g2s(ring + s * kF8Stage, a + static_cast<size_t>(kb) * abytes, abytes, &full[s]);
+          bulk_g2s_hint(ring + s * kF8Stage, a + static_cast<size_t>(kb) * abytes, abytes, &full[s], wpol);
           bulk_g2s(ring + s * kF8Stage + kF8ABytes, b + static_cast<size_t>(kb) * kF8BBytes,
                    kF8BBytes, &full[s]);
         }

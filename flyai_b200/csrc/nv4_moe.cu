@@ -272,6 +272,9 @@ __global__ void __launch_bounds__(kNvThreads, 1) nv4_moe_kernel(const __grid_con
 
   if (warp == 0) {
     // ---------------- producer ----------------
+    // weights are read once: evict-first L2 policy (they recycle each other's
+    // lines instead of evicting what else the L2 holds)
+    const uint64_t wpol = l2_policy_evict_first();
     bool ok = true;
     uint32_t ks = 0;
     for (; cur.valid(); cur.next()) {
@@ -295,7 +298,7 @@ __global__ void __launch_bounds__(kNvThreads, 1) nv4_moe_kernel(const __grid_con
               break;
             }
             mbar_expect_tx(&full[s], abytes + kNvBBytes);
-            bulk_g2s(ring + s * kNvStage, a + static_cast<size_t>(kb) * abytes, abytes, &full[s]);
+            bulk_g2s_hint(ring + s * kNvStage, a + static_cast<size_t>(kb) * abytes, abytes, &full[s], wpol);
           }
           if (!wait_counter_geq(&p.chunk_done[t.chunk], NI)) ok = false;
           fence_proxy_async_global();
@@ -312,7 +315,7 @@ __global__ void __launch_bounds__(kNvThreads, 1) nv4_moe_kernel(const __grid_con
             break;
           }
           mbar_expect_tx(&full[s], abytes + kNvBBytes);
-          bulk_g2s(ring + s * kNvStage, a + static_cast<size_t>(kb) * abytes, abytes, &full[s]);
+          bulk_g2s_hint(ring + s * kNvStage, a + static_cast<size_t>(kb) * abytes, abytes, &full[s], wpol);
           bulk_g2s(ring + s * kNvStage + kNvABytes, b + static_cast<size_t>(kb) * kNvBBytes,
                    kNvBBytes, &full[s]);
         }

@@ -355,6 +355,9 @@ __global__ void __launch_bounds__(kV4Threads, 1) v4_moe_kernel(const __grid_cons
 
   if (warp == 0) {
     // ---------------- producer ----------------
+    // weights are read once: evict-first L2 policy (they recycle each other's
+    // lines instead of evicting what else the L2 holds)
+    const uint64_t wpol = l2_policy_evict_first();
     bool ok = true;
     uint32_t ks = 0;
     for (; cur.valid(); cur.next()) {
@@ -382,7 +385,7 @@ __global__ void __launch_bounds__(kV4Threads, 1) v4_moe_kernel(const __grid_cons
               break;
             }
             mbar_expect_tx(&raw_full[s], abytes + kV4BBytes);
-            bulk_g2s(raw + s * kV4Stage, a + static_cast<size_t>(kb) * abytes, abytes, &raw_full[s]);
+            bulk_g2s_hint(raw + s * kV4Stage, a + static_cast<size_t>(kb) * abytes, abytes, &raw_full[s], wpol);
           }
           if (!wait_counter_geq(&p.chunk_done[t.chunk], NI)) ok = false;
           fence_proxy_async_global();
@@ -400,7 +403,7 @@ __global__ void __launch_bounds__(kV4Threads, 1) v4_moe_kernel(const __grid_cons
             break;
           }
           mbar_expect_tx(&raw_full[s], abytes + kV4BBytes);
-          bulk_g2s(raw + s * kV4Stage, a + static_cast<size_t>(kb) * abytes, abytes, &raw_full[s]);
+          bulk_g2s_hint(raw + s * kV4Stage, a + static_cast<size_t>(kb) * abytes, abytes, &raw_full[s], wpol);
           bulk_g2s(raw + s * kV4Stage + kV4BOff, b + static_cast<size_t>(kb) * kV4BBytes, kV4BBytes,
                    &raw_full[s]);
         }
