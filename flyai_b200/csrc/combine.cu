@@ -2,7 +2,7 @@
 // token's k weighted expert rows in ascending expert id with a bf16 rounding
 // after every add -- the order and rounding of the reference's index_add_ loop
 // (transformers/models/gpt_oss/modeling_gpt_oss.py:96-112).  One CTA per
-// (token, 512 output columns), launched with programmatic dependent launch
+// (token, 2048 output columns), launched with programmatic dependent launch
 // behind the expert kernel.
 #include "common.cuh"
 #include "route.cuh"
@@ -10,19 +10,35 @@
 
 namespace flyai {
 
+// Columns [o, o + 8) of token m: every slot's 8 values loaded before the folds.
 __device__ __forceinline__ void fold_rows(const uint16_t* __restrict__ rows, const int* order,
                                           int m, int k, int H, bool live, uint16_t* __restrict__ y) {
-  for (int o = (blockIdx.y * blockDim.x + threadIdx.x) * 2; o < H; o += gridDim.y * blockDim.x * 2) {
-    float a0 = 0.f, a1 = 0.f;
-    for (int s = 0; s < k && live; ++s) {
-      const uint32_t v = __ldcg(reinterpret_cast<const uint32_t*>(
-          rows + (static_cast<size_t>(m) * k + order[s]) * H + o));
-      a0 = bf16r(__fadd_rn(a0, __uint_as_float(v << 16)));
-      a1 = bf16r(__fadd_rn(a1, __uint_as_float(v & 0xFFFF0000u)));
+  for (int o = (blockIdx.y * blockDim.x + threadIdx.x) * 8; o < H; o += gridDim.y * blockDim.x * 8) {
+    uint32_t v[kMaxTopK][4];
+#pragma unroll
+    for (int s = 0; s < kMaxTopK; ++s)
+      if (s < k && live) {
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(
+            rows + (static_cast<size_t>(m) * k + order[s]) * H + o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[s][j] = __ldcg(src + j);
+      }
+    uint32_t out[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int s = 0; s < kMaxTopK; ++s)
+        if (s < k && live) {
+          a0 = bf16r(__fadd_rn(a0, __uint_as_float(v[s][j] << 16)));
+          a1 = bf16r(__fadd_rn(a1, __uint_as_float(v[s][j] & 0xFFFF0000u)));
+        }
+      out[j] = static_cast<uint32_t>(float_to_bf16_bits(a0)) |
+               (static_cast<uint32_t>(float_to_bf16_bits(a1)) << 16);
     }
-    *reinterpret_cast<uint32_t*>(y + static_cast<size_t>(m) * H + o) =
-        static_cast<uint32_t>(float_to_bf16_bits(a0)) |
-        (static_cast<uint32_t>(float_to_bf16_bits(a1)) << 16);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(y + static_cast<size_t>(m) * H + o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = out[j];
   }
 }
 
@@ -82,7 +98,7 @@ __global__ void __launch_bounds__(256) combine_ep_kernel(const uint16_t* __restr
 static cudaError_t launch_fold(const flyai_moe_desc& d, int M, cudaStream_t stream, void (*kern)(),
                                void** args) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(M, (d.hidden + 511) / 512);
+  cfg.gridDim = dim3(M, (d.hidden + 2047) / 2048);   // 8 columns per thread
   cfg.blockDim = dim3(256);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

@@ -234,6 +234,7 @@ __host__ __device__ inline int tc_pf_max_chunks(size_t P, size_t El) {
   return static_cast<int>((El < P ? El : P) + P / kTcPfChunk + 1);
 }
 constexpr int kTerms = 6;        // e2m1 terms an activation row is split into for kind::mxf4
+constexpr int kNpLogitSlices = 8;   // K slices of the prefill router logits (fp64 partial sums)
 
 // ---- workspace layout -------------------------------------------------------
 // Words of the route ticket region (the first 512 bytes of the workspace in
@@ -274,6 +275,8 @@ struct Workspace {
   uint8_t* phb;        // prefill only: [pf_max_chunks][I/64][kTcPfBlk] bf16 SwiGLU rows by chunk
   int32_t* pcf;        // prefill only: [pf_max_chunks][kTcPfChunk] flat pair index per chunk slot
   float* pcw;          // prefill only: [pf_max_chunks][kTcPfChunk] routing weight per chunk slot
+  double* plog;        // prefill only: [kNpLogitSlices][M, E] fp64 partial router logits
+  float* pxm;          // prefill only: [kNpLogitSlices][M] partial row maxima of |x| (unused)
   int pf_max_chunks;
   int4* chunk_info;    // [max_chunks] (local expert, first permuted position, tokens, 0)
   int32_t* chunk_rows; // [max_chunks][kChunkRowStride] token row of each of the chunk's tokens
@@ -331,6 +334,8 @@ inline Workspace carve_workspace(const flyai_moe_desc& d, int M, void* base) {
         take(static_cast<size_t>(w.pf_max_chunks) * (d.inter / kTcPfK) * kTcPfBlk));
     w.pcf = reinterpret_cast<int32_t*>(take(static_cast<size_t>(w.pf_max_chunks) * kTcPfChunk * 4));
     w.pcw = reinterpret_cast<float*>(take(static_cast<size_t>(w.pf_max_chunks) * kTcPfChunk * 4));
+    w.plog = reinterpret_cast<double*>(take(static_cast<size_t>(kNpLogitSlices) * M * E * 8));
+    w.pxm = reinterpret_cast<float*>(take(static_cast<size_t>(kNpLogitSlices) * M * 4));
   }
   w.chunk_info = reinterpret_cast<int4*>(take(static_cast<size_t>(w.max_chunks) * 16));
   w.chunk_rows = reinterpret_cast<int32_t*>(take(static_cast<size_t>(w.max_chunks) * kChunkRowStride * 4));

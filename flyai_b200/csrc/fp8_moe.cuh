@@ -26,7 +26,6 @@ constexpr int kNvPfMaxTokens = 8192;
 constexpr int kNpChunk = 128;
 constexpr int kNpK = 64;                          // K elements per slice / pipeline stage
 constexpr int kNpBlk = kNpChunk * kNpK * 2;       // 16 KB: one slice of a full chunk
-constexpr int kNpLogitSlices = 8;                 // K slices of the prefill router logits
 __host__ __device__ inline int nvp_max_chunks(int El, int P) {
   return (El < P ? El : P) + P / kNpChunk + 1;
 }
@@ -195,6 +194,14 @@ int launch_fp8_select(const flyai_moe_desc& d, int M, const flyai_moe_weights& w
 // NVFP4 prefill (M > kF8MaxTokens): router logits, selection, plan of kNpChunk-pair
 // chunks and the chunks' bf16 token rows; then the expert kernel (and the fold
 // into y when y is not null).
+// Prefill router logits (nv4_prefill.cu): fp64 partial dot products of
+// kLgTok-token x kLgExp-expert tiles over kNpLogitSlices K slices -- part
+// [slice][M][E] -- and the slices' |x| row maxima.  Grid (ceil(E/kLgExp),
+// ceil(M/kLgTok), kNpLogitSlices) x 256 threads; H a multiple of 32.
+constexpr int kLgTok = 64, kLgExp = 128;
+__global__ void nvp_logits_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, int M,
+                                  int E, int H, double* __restrict__ part, float* __restrict__ xmax_part);
+
 int launch_nvp_route(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_weights& w,
                      float* logits, int32_t* topk_ids, float* topk_weights,
                      const Fp8Workspace& ws, cudaStream_t stream, const void* logits_in = nullptr);

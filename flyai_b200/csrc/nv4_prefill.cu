@@ -80,7 +80,7 @@ static cudaError_t np_launch(Kern kernel, dim3 grid, int block, size_t smem, cud
 // kernel computes -- rounded once to fp32 and once to bf16.  The same pass takes
 // each token row's |x| maximum for the f16 row factor.
 // ---------------------------------------------------------------------------
-constexpr int kLgTok = 64, kLgExp = 128, kLgK = 32, kLgSlices = kNpLogitSlices;
+constexpr int kLgK = 32, kLgSlices = kNpLogitSlices;
 
 __global__ void __launch_bounds__(256) nvp_logits_kernel(const uint16_t* __restrict__ x,
                                                          const uint16_t* __restrict__ w, int M,

@@ -9,30 +9,29 @@
 #include "route.cuh"
 #include "terms.cuh"
 #include "route_dev.cuh"
+#include "fp8_moe.cuh"
 
 namespace flyai {
 
-// 1) logits: logit_warp (route_dev.cuh), one warp per (token, expert).
-__global__ void __launch_bounds__(256) route_logits_kernel(const uint16_t* __restrict__ x,
-                                                           const uint16_t* __restrict__ wr,
-                                                           const uint16_t* __restrict__ br,
-                                                           int M, int E, int H,
-                                                           float* __restrict__ logits,
-                                                           uint16_t* __restrict__ logits_out,
-                                                           uint8_t* __restrict__ x_terms,
-                                                           uint8_t* __restrict__ x_sf) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m = blockIdx.y;
-  const int e = blockIdx.x * 8 + warp;
-  // the token's e2m1 terms for the tensor-core expert kernels, once per token
-  if (x_terms && blockIdx.x == 0)
-    decompose_rows(x, H, H, m, 1, x_terms + static_cast<size_t>(m) * term_row_bytes(H),
-                   x_sf + static_cast<size_t>(m) * term_sf_row_bytes(H));
-  if (m >= M || e >= E) return;
-  const float v = logit_warp(x, wr, br, m, e, H);
-  if (lane == 0) {
-    logits[static_cast<size_t>(m) * E + e] = v;
-    if (logits_out) logits_out[static_cast<size_t>(m) * E + e] = float_to_bf16_bits(v);
+// 1) logits.  Verify sizes: logit_warp (route_dev.cuh) inside route_fused_kernel
+// and the fused expert kernel.  Prefill sizes: nvp_logits_kernel's fp64 partial
+// sums over K slices (a register-tiled DFMA product; bf16 products are exact in
+// fp64), added here in slice order with the bias and rounded once to fp32 and
+// once to bf16 -- the value logit_warp computes, to fp64 rounding of the sum.
+__global__ void __launch_bounds__(256) route_logits_sum_kernel(const double* __restrict__ part,
+                                                               const uint16_t* __restrict__ br, int M,
+                                                               int E, float* __restrict__ logits,
+                                                               uint16_t* __restrict__ logits_out) {
+  const size_t n = static_cast<size_t>(M) * E;
+  for (size_t u = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; u < n;
+       u += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    double a = part[u];
+#pragma unroll
+    for (int s = 1; s < kNpLogitSlices; ++s) a += part[s * n + u];
+    if (br) a += static_cast<double>(bf16_bits_to_float(br[u % E]));
+    const float v = bf16r(__double2float_rn(a));
+    logits[u] = v;
+    if (logits_out) logits_out[u] = float_to_bf16_bits(v);
   }
 }
 
@@ -450,12 +449,13 @@ int launch_route(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_
     return st == cudaSuccess ? FLYAI_OK : FLYAI_ERR_CUDA;
   }
   if (M > 0) {
-    dim3 grid((E + 7) / 8, M);
-    route_logits_kernel<<<grid, 256, 0, stream>>>(
-        static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(w.router_w),
-        static_cast<const uint16_t*>(w.router_b), M, E, H, ws.logits,
-        static_cast<uint16_t*>(logits_out), tc && M < kTcPrefillMinTokens ? ws.x_terms : nullptr,
-        tc && M < kTcPrefillMinTokens ? ws.x_sf : nullptr);   // prefill splits x after the plan
+    if (!ws.plog) return FLYAI_ERR_UNSUPPORTED;   // batches above 64 tokens carve the partials
+    nvp_logits_kernel<<<dim3((E + kLgExp - 1) / kLgExp, (M + kLgTok - 1) / kLgTok, kNpLogitSlices), 256, 0,
+                        stream>>>(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(w.router_w), M,
+                                  E, H, ws.plog, ws.pxm);
+    note_launch();
+    route_logits_sum_kernel<<<4 * 148, 256, 0, stream>>>(ws.plog, static_cast<const uint16_t*>(w.router_b), M, E,
+                                                         ws.logits, static_cast<uint16_t*>(logits_out));
     note_launch();
     const size_t smem = 8 * (static_cast<size_t>(E) * sizeof(KV) + kTopkWarpScratch);
     route_select_softmax_kernel<<<(M + 7) / 8, 256, smem, stream>>>(

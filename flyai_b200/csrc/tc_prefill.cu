@@ -21,8 +21,10 @@
 // gp_moe_kernel, 736 threads:
 //   warp 0      weight producer: per 128-wide K step of an item, bulk copies of
 //               its bank tiles (e2m1 data + e8m0 scale chunk) into a ring of 4;
-//   warp 1      MMA issuer: 4 kind::f16 MMAs (K = 16) per tile and slice into one
-//               of two 256-column TMEM slots (tile t at +128 t);
+//   warps 1, 23 MMA issuers, one per tile of an item: 4 kind::f16 MMAs (K = 16)
+//               per tile and slice into one of two 256-column TMEM slots (tile t
+//               at +128 t); two issuers double the instruction rate that bounds
+//               the small-N MMAs of partly filled chunks;
 //   warps 2..5  epilogue: gate/up -> bias, clamp, SwiGLU in bf16 straight into
 //               the chunk's down operand (chunk_done counts the items); down ->
 //               bias, routing weight, bf16 pair rows by flat pair index;
@@ -32,7 +34,8 @@
 //               SwiGLU rows) into a ring of 5.
 // A gate/up item is two consecutive 128-row tiles of the interleaved W13 (even
 // rows gate, odd rows up): 128 SwiGLU features; the epilogue pairs TMEM lanes
-// 2j, 2j+1.  A down item is one 128-row tile of W2.  Both operands use the
+// 2j, 2j+1.  A down item is two consecutive 128-row tiles of W2 (the last item
+// of a projection may hold one).  Both operands use the
 // 128-byte swizzle (tc::smem_desc_sw128).  Every wait is bounded (~2 s) and
 // records kErrWaitTimeout.
 #include <cuda_bf16.h>
@@ -58,7 +61,8 @@ constexpr int kGpBStages = 5;
 constexpr int kGpDqWarps = 16;
 constexpr int kGpDqThreads = kGpDqWarps * 32;
 constexpr int kGpRowWarp = 6 + kGpDqWarps;        // the row producer
-constexpr int kGpThreads = (kGpRowWarp + 1) * 32;
+constexpr int kGpMmaWarp2 = kGpRowWarp + 1;       // the second MMA issuer (an item's tile 1)
+constexpr int kGpThreads = (kGpMmaWarp2 + 1) * 32;
 constexpr int kGpSlotCols = 256;
 constexpr int kGpOffA = kGpRaw * kGpRawBytes;
 constexpr int kGpOffB = kGpOffA + kGpAStages * kGpAStage;
@@ -249,14 +253,14 @@ __global__ void __launch_bounds__(kGpThreads, 1) gp_moe_kernel(const __grid_cons
     }
     for (int s = 0; s < SA; ++s) {
       mbar_init(&a_full[s], kGpDqWarps / 2);   // the slot's expansion group
-      mbar_init(&a_empty[s], 1);
+      mbar_init(&a_empty[s], 2);               // both issuers' MMAs of the slice
     }
     for (int s = 0; s < SB; ++s) {
       mbar_init(&b_full[s], 1);
-      mbar_init(&b_empty[s], 1);
+      mbar_init(&b_empty[s], 2);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_full[b], 2);
       mbar_init(&acc_empty[b], 4);
     }
     mbar_init(epi_done, 4);
@@ -274,7 +278,7 @@ __global__ void __launch_bounds__(kGpThreads, 1) gp_moe_kernel(const __grid_cons
 
   const TcLayout& L13 = p.gu.L;
   const TcLayout& L2 = p.dn.L;
-  const int NI = (L13.MT + 1) / 2, NT = L2.MT;   // gate/up items of two tiles, down items of one
+  const int NI = (L13.MT + 1) / 2, NT = (L2.MT + 1) / 2;   // items of two tiles
   const int KS1 = p.hidden / kGpK, KS2 = p.inter / kGpK;
   TcStridedCursor cur;   // concurrent CTAs share a chunk's rows and an expert's weights in L2
   cur.start(blockIdx.x, gridDim.x, *p.n_chunks, NI, NT);
@@ -292,8 +296,8 @@ __global__ void __launch_bounds__(kGpThreads, 1) gp_moe_kernel(const __grid_cons
         const TcItem t = cur.t;
         const int e = __ldg(&p.chunk_info[t.chunk].x);
         const TcLayout& L = t.gu ? L13 : L2;
-        const int mt0 = t.gu ? 2 * t.mt : t.mt;
-        const int tiles = t.gu ? min(2, L.MT - mt0) : 1;
+        const int mt0 = 2 * t.mt;
+        const int tiles = min(2, L.MT - mt0);
         const uint8_t* ebase = (t.gu ? p.gu.bank : p.dn.bank) + static_cast<size_t>(e) * L.expert_bytes;
         GpSteps st;
         for (st.start(L.K); st.valid(); st.next(), ++rr) {
@@ -362,10 +366,13 @@ __global__ void __launch_bounds__(kGpThreads, 1) gp_moe_kernel(const __grid_cons
       if (!ok) atomicOr(p.err, kErrWaitTimeout);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    // The whole warp walks the items and waits (operands stay warp-uniform); one
-    // elected lane issues the tcgen05 instructions.
+  } else if (warp == 1 || warp == kGpMmaWarp2) {
+    // ---------------- MMA issuers ----------------
+    // Issuer `me` multiplies tile `me` of every item (an item with one tile
+    // leaves the second issuer only its commits).  The whole warp walks the
+    // items and waits (operands stay warp-uniform); one elected lane issues the
+    // tcgen05 instructions.
+    const int me = warp == 1 ? 0 : 1;
     bool ok = true;
     uint32_t ks = 0, item = 0, ause[2] = {0u, 0u};
     const uint64_t a0 = tc::smem_desc_sw128(sa), b0 = tc::smem_desc_sw128(sb);
@@ -374,7 +381,7 @@ __global__ void __launch_bounds__(kGpThreads, 1) gp_moe_kernel(const __grid_cons
       const int np = (__ldg(&p.chunk_info[t.chunk].z) + 15) & ~15;
       const uint32_t idesc = tc::idesc_bf16(np);
       const TcLayout& L = t.gu ? L13 : L2;
-      const int tiles = t.gu ? min(2, L.MT - 2 * t.mt) : 1;
+      const bool mine = me < min(2, L.MT - 2 * t.mt);
       const uint32_t slot = item & 1u;
       if (item >= 2) ok = mbar_wait_bounded(&acc_empty[slot], ((item >> 1) - 1) & 1);
       ok = __all_sync(0xffffffffu, ok);
@@ -391,11 +398,12 @@ __global__ void __launch_bounds__(kGpThreads, 1) gp_moe_kernel(const __grid_cons
           tc::fence_after_sync();
           const uint64_t as = a0 + ((h * kGpAStage) >> 4), bs = b0 + ((u * kGpBlk) >> 4);
           if (elect_one()) {
-            for (int tt = 0; tt < tiles; ++tt)
+            if (mine) {
 #pragma unroll
               for (int i = 0; i < 4; ++i)   // K = 16 per MMA: 32 bytes into each 128-byte line
-                tc::mma_kf16(d + tt * 128, as + ((tt * kGpATile + i * 32) >> 4), bs + i * 2, idesc,
+                tc::mma_kf16(d + me * 128, as + ((me * kGpATile + i * 32) >> 4), bs + i * 2, idesc,
                              !first || i > 0);
+            }
             tc::commit_to(&a_empty[h]);
             tc::commit_to(&b_empty[u]);
           }
@@ -412,8 +420,10 @@ __global__ void __launch_bounds__(kGpThreads, 1) gp_moe_kernel(const __grid_cons
       if (!ok) atomicOr(p.err, kErrWaitTimeout);
     }
     __syncwarp();
-    tc::fence_after_sync();
-    tc::tmem_dealloc(tbase, 512);
+    if (me == 0) {
+      tc::fence_after_sync();
+      tc::tmem_dealloc(tbase, 512);
+    }
   } else if (warp < 6) {
     // ---------------- epilogue (TMEM lane quadrant = warp % 4) ----------------
     const int q = warp & 3, m = 32 * q + lane;   // row of the 128-row tile
@@ -460,14 +470,17 @@ __global__ void __launch_bounds__(kGpThreads, 1) gp_moe_kernel(const __grid_cons
           }
         }
       } else {
-        const int row = t.mt * 128 + m;   // output column of the pair rows
-        const bool live_row = row < L2.R;
-        const float bias_v = (p.dn.bias && live_row) ? __ldg(p.dn.bias + static_cast<size_t>(e) * L2.R + row) : 0.f;
         const int32_t* cfl = p.cf + static_cast<size_t>(t.chunk) * kGpN;
         const float* cwt = p.cw + static_cast<size_t>(t.chunk) * kGpN;
+        const int tiles = min(2, L2.MT - 2 * t.mt);
+        for (int tt = 0; tt < tiles; ++tt) {
+        const int row = (2 * t.mt + tt) * 128 + m;   // output column of the pair rows
+        const bool live_row = row < L2.R;
+        const float bias_v =
+            (p.dn.bias && live_row) ? __ldg(p.dn.bias + static_cast<size_t>(e) * L2.R + row) : 0.f;
         for (int c0 = 0; c0 < np; c0 += 16) {
           uint32_t v[16];
-          tc::tmem_ld16(ta + c0, v);
+          tc::tmem_ld16(ta + tt * 128 + c0, v);
           int fl[16];
           float wt[16];
 #pragma unroll
@@ -487,6 +500,7 @@ __global__ void __launch_bounds__(kGpThreads, 1) gp_moe_kernel(const __grid_cons
               p.pair_out[static_cast<size_t>(fl[j]) * p.hidden + row] = float_to_bf16_bits(o);
             }
           }
+        }
         }
       }
       tc::fence_before_sync();
@@ -518,8 +532,8 @@ __global__ void __launch_bounds__(kGpThreads, 1) gp_moe_kernel(const __grid_cons
     for (; cur.valid(); cur.next()) {
       const TcItem t = cur.t;
       const TcLayout& L = t.gu ? L13 : L2;
-      const int mt0 = t.gu ? 2 * t.mt : t.mt;
-      const int tiles = t.gu ? min(2, L.MT - mt0) : 1;
+      const int mt0 = 2 * t.mt;
+      const int tiles = min(2, L.MT - mt0);
       GpSteps st;
       for (st.start(L.K); st.valid(); st.next(), ++rr) {
         const uint32_t r = rr % R;
