@@ -390,7 +390,7 @@ def main():
         "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": hbm_peak,
                      "unit": "GB/s", "frac": round(achieved_gbs / hbm_peak, 4),
                      "traffic": profiled_traffic(world, M, args.seed),
-                     "kernel": "tc_moe_kernel (gate/up + down of one layer call, one launch)",
+                     "kernel": "tc_moe_kernel<true> (route + gate/up + down + fold: the whole layer call, one launch)" if world == 1 else "tc_moe_kernel (gate/up + down of this rank's experts)",
                      "kernel_us": round(exp_ms * 1e3, 2),
                      "bytes_per_launch": bytes_local, "distinct_experts": distinct,
                      "peak_source": peak_kind,

@@ -190,9 +190,15 @@ constexpr int kNvSfBase = kNvSlots * kNvSlotCols;
 constexpr int kNvThreads = 224;              // warp 0 producer, 1 and 6 MMA issuers, 2..5 epilogue
 static_assert(kNvStage % 16 == 0, "stage alignment");
 static_assert(kNvSfBase + kNvStages * kNvSfCols <= 512, "tensor memory budget");
-// An even stage count keeps every use of a stage on the same issuer warp (K blocks
-// alternate issuers by ks parity); an odd count has not been shown safe.
-static_assert(kNvStages % 2 == 0, "even number of stages");
+// Each issuer waits only for the stages of its own K blocks (ks parity), by
+// phase parity.  With an even stage count stage s = ks % S always carries K
+// blocks of one parity, so an issuer waits for every use of its stages in order.
+// With an odd count consecutive uses of a stage alternate between the issuers:
+// an issuer then waits for use k+2 of a stage whose use k+1 (the other
+// issuer's) may not have landed, and phase k+2 has the parity of phase k, which
+// it already saw complete -- the wait passes early, the MMAs read a stage in
+// mid-copy and the ring's phases fall out of step.
+static_assert(kNvStages % 2 == 0, "stage s must carry K blocks of one issuer parity");
 static_assert(kNvDnGroup * kNvN <= kNvSlotCols && 4 * kNvN <= kNvSlotCols, "slot layout");
 
 struct NvParams {

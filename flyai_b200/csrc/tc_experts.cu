@@ -107,7 +107,14 @@ int launch_tc_pack(const flyai_moe_desc& d, int proj, const void* blocks, const 
 constexpr int kTcN = kTcChunk * kTermSlots;                // 32: MMA N, column token*8 + term
 constexpr int kTcAcc = 4;                                  // accumulator buffers
 constexpr int kTcAccCols = 2 * kTcN;                       // even / odd K-tile halves
+// The ring's stages are split between the two MMA issuers (issuer p: stages p,
+// p + 2, ...; K-tile kt goes to issuer kt & 1), so every use of a stage is
+// waited for by the one issuer that consumes it, in order.  (A stage shared by
+// the issuers would let one of them wait for a use two phases after the last
+// one it saw, which a parity wait cannot tell from that last phase.)
 constexpr int kTcStages = 4;
+constexpr int kTcHalfStages = kTcStages / 2;
+static_assert(kTcStages % 2 == 0, "the ring splits evenly between the two issuers");
 constexpr int kTcRun = 3;                                  // items per dealt run (TcRunCursor)
 constexpr int kTcSfaCol = kTcAcc * kTcAccCols;             // A scales: 16 columns per ring stage
 constexpr int kTcSfbCol = kTcSfaCol + 16 * kTcStages;      // B scales: 2 buffers x 4 per K group
@@ -526,7 +533,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
     // so they recycle each other's L2 lines instead of evicting (and writing
     // back) whatever else the L2 holds.
     bool ok = true;
-    uint32_t li = 0;
+    uint32_t nuse[2] = {0u, 0u};   // tiles put into each issuer's half of the ring
     const uint64_t stream_policy = l2_policy_evict_first();
     for (; cur.valid(); cur.next()) {
       if (lane == 0 && ok) {
@@ -536,8 +543,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
         const int rows_t = tc_rows(P.L, t.mt);
         const uint8_t* src =
             P.bank + static_cast<size_t>(e) * P.L.expert_bytes + static_cast<size_t>(t.mt) * P.L.mtile_full;
-        for (int kt = 0; kt < P.L.NKT; ++kt, ++li) {
-          const uint32_t s = li % S, use = li / S;
+        for (int kt = 0; kt < P.L.NKT; ++kt) {
+          const uint32_t par = kt & 1, k = nuse[par]++;
+          const uint32_t s = par + 2 * (k % kTcHalfStages), use = k / kTcHalfStages;
           if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1)) {
             ok = false;
             break;
@@ -551,10 +559,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
       __syncwarp();
     }
     if (lane == 0) {
-      for (uint32_t s = 0; s < S && s < li; ++s) {   // copies in flight land before exit
-        const uint32_t last = ((li - 1 - s) / S) * S + s;
-        if (!mbar_wait_bounded(&full[s], (last / S) & 1)) ok = false;
-      }
+      for (uint32_t par = 0; par < 2; ++par)   // copies in flight land before exit
+        for (uint32_t j = 0; j < kTcHalfStages && j < nuse[par]; ++j) {
+          const uint32_t last = ((nuse[par] - 1 - j) / kTcHalfStages) * kTcHalfStages + j;
+          if (!mbar_wait_bounded(&full[par + 2 * j], (last / kTcHalfStages) & 1)) ok = false;
+        }
       if (!ok) tc_record_timeout(p);
     }
     __syncwarp();
@@ -568,7 +577,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
     // to their address field (smem addresses < 256 KB never carry out of it).
     const int odd = warp == 7;
     bool ok = true;
-    uint32_t li = 0, item_no = 0, bc = 0;
+    uint32_t nuse = 0, item_no = 0, bc = 0;   // nuse: tiles of this issuer so far
     TcItem prev{-1, -1, -1};
     const uint32_t idesc[2] = {tc::idesc_mxf4(kTcN, 0, 0), tc::idesc_mxf4(kTcN, 2, 2)};
     const uint64_t cp_ring = tc::smem_desc_kmajor(ring, 0, 128);
@@ -615,10 +624,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
       const uint32_t d_tmem = tbase + buf * kTcAccCols + odd * kTcN;
       const uint64_t a_base = tc::smem_desc_kmajor(ring, rows_t * 16, 128);
       const uint32_t a_step = static_cast<uint32_t>(rows_t) * 2;   // two 16-byte K chunks
-      for (int kt = 0; kt < P.L.NKT; ++kt, ++li) {
+      for (int kt = 0; kt < P.L.NKT; ++kt) {
         if ((kt & 1) != odd) continue;
-        const uint32_t s = li % S;
-        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (li / S) & 1));
+        const uint32_t k = nuse++;
+        const uint32_t s = odd + 2 * (k % kTcHalfStages);
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (k / kTcHalfStages) & 1));
         if (!ok) break;
         tc::fence_after_sync();
         const int kt_len = tc_kt_len(P.L, kt);
