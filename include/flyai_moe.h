@@ -188,7 +188,7 @@ FLYAI_API int flyai_moe_pack_shared_fp8(const flyai_moe_desc* desc, int32_t proj
 /* Workspace bytes for calls with up to desc->max_tokens tokens.  The layout
  * depends only on the descriptor, so one workspace serves every call with
  * num_tokens <= max_tokens.  Zero-fill a workspace once before its first use:
- * its first 268 bytes are counters the kernels keep and restore to zero after
+ * its first 276 bytes are counters the kernels keep and restore to zero after
  * every call (also when the workspace is reused with another descriptor). */
 FLYAI_API int flyai_moe_workspace_bytes(const flyai_moe_desc* desc, size_t* bytes);
 
@@ -307,7 +307,13 @@ FLYAI_API int flyai_moe_combine_ep(const flyai_moe_desc* desc, int32_t num_token
                                    size_t workspace_bytes, void* stream);
 
 /* The whole layer: route + experts.  GptOssMLP.forward(hidden) -> (out, router_scores)
- * (modeling_gpt_oss.py:140-146): y = out, topk_weights = router_scores. */
+ * (modeling_gpt_oss.py:140-146): y = out, topk_weights = router_scores.
+ * MXFP4 layers of 1..64 tokens with at most 256 (token, slot) pairs on a GPU
+ * holding every expert run as ONE cooperative launch (routing, experts and the
+ * fold into y; one CTA per SM, which must all be resident: on a GPU whose SMs
+ * are partly held by other work the launch fails with FLYAI_ERR_CUDA instead of
+ * waiting); that path leaves topk ids/weights in the workspace but not the
+ * histogram and permutation flyai_moe_read_plan returns after flyai_moe_route. */
 FLYAI_API int flyai_moe_forward(const flyai_moe_desc* desc, int32_t num_tokens, const void* x,
                       const flyai_moe_weights* w, void* y, int32_t* topk_ids,
                       void* topk_weights, void* workspace, size_t workspace_bytes,
