@@ -278,7 +278,8 @@ def main():
     ep = None
     if world > 1:
         from flyai_b200.ep import ExpertParallelMoE
-        ep = ExpertParallelMoE(moe, p2p=not args.ep_nccl)
+        # tokens replicated on every rank (the reference's expert-parallel pattern)
+        ep = ExpertParallelMoE(moe, p2p=not args.ep_nccl, broadcast=False)
 
     def layer_step(xin, yout):
         if world == 1:
@@ -331,13 +332,16 @@ def main():
     w_h = torch.empty(M, K_TOP, dtype=torch.bfloat16).pin_memory()
     x_in = torch.empty_like(x)
 
+    ids_d = torch.empty(M, K_TOP, dtype=torch.int32, device=dev)
+    wts_d = torch.empty(M, K_TOP, dtype=torch.bfloat16, device=dev)
+
     def e2e_step():
         x_in.copy_(x_h, non_blocking=True)
         if world == 1:
             _, _, wts = moe.forward(x_in, out=y)
         else:
-            layer_step(x_in, y)
-            _, _, wts = moe.route(x_in, logits=False)
+            ep.forward(x_in, out=y, ids=ids_d, wts=wts_d)
+            wts = wts_d
         y_h.copy_(y, non_blocking=True)
         w_h.copy_(wts, non_blocking=True)
     e2e_ms, _ = timed(e2e_step, args.steps, args.warmup)
@@ -382,7 +386,8 @@ def main():
         "data": "synthetic (seeded; BASELINE config 1 distributions)",
         "config": {"workload": "gpt-oss-120b MoE layer verify M=5 (config 1)", "experts": E,
                    "top_k": K_TOP, "hidden": H, "inter": I, "tokens": M,
-                   "parallelism": f"ep{world}", "l2": "flushed (256 MiB write) before every timed step"},
+                   "parallelism": f"ep{world}", "l2": "flushed (256 MiB write) before every timed step",
+                   **({"ep_tokens": "replicated on every rank"} if world > 1 else {})},
         "e2e": {"value": round(e2e_ms * 1e3, 2), "unit": "us", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,

@@ -39,7 +39,7 @@ EXPORTS = (
     "flyai_moe_forward", "flyai_moe_launch_count", "flyai_moe_read_plan",
     "flyai_moe_set_profile_events", "flyai_moe_ep_mailbox_bytes", "flyai_moe_ep_alloc",
     "flyai_moe_ep_free", "flyai_moe_ipc_get_handle", "flyai_moe_ipc_open", "flyai_moe_ipc_close",
-    "flyai_moe_experts_ep", "flyai_moe_combine_ep",
+    "flyai_moe_experts_ep", "flyai_moe_combine_ep", "flyai_moe_forward_ep",
     "flyai_moe_forward_noalloc", "flyai_moe_read_error", "flyai_moe_pack_fp8",
     "flyai_moe_pack_nvfp4", "flyai_moe_pack_fp4", "flyai_moe_pack_shared_fp8",
     "flyai_moe_route_hash", "flyai_moe_route_logits",
@@ -121,6 +121,7 @@ def load():
         "flyai_moe_ipc_open": ([vp, ctypes.POINTER(vp)], ctypes.c_int),
         "flyai_moe_ipc_close": ([vp], ctypes.c_int),
         "flyai_moe_experts_ep": ([pd, i32, vp, pw, ctypes.POINTER(EpPeers), vp, sz, vp], ctypes.c_int),
+        "flyai_moe_forward_ep": ([pd, i32, vp, pw, ctypes.POINTER(EpPeers), vp, vp, vp, sz, vp], ctypes.c_int),
         "flyai_moe_combine_ep": ([pd, i32, ctypes.POINTER(EpPeers), vp, vp, sz, vp], ctypes.c_int),
         "flyai_moe_read_plan": ([pd, i32, vp, sz, vp, vp, vp, vp], ctypes.c_int),
         "flyai_moe_forward_noalloc": ([pd, i32, vp, pw, vp, vp, vp, vp], ctypes.c_int),

@@ -565,6 +565,26 @@ int flyai_moe_experts_ep(const flyai_moe_desc* desc, int32_t M, const void* x,
   return st;
 }
 
+int flyai_moe_forward_ep(const flyai_moe_desc* desc, int32_t M, const void* x,
+                         const flyai_moe_weights* w, const flyai_moe_ep_peers* peers, int32_t* topk_ids,
+                         void* topk_weights, void* workspace, size_t workspace_bytes, void* stream) {
+  FLYAI_TRY(check_desc(desc));
+  FLYAI_TRY(check_tokens(desc, M));
+  FLYAI_TRY(check_workspace(desc, workspace, workspace_bytes));
+  FLYAI_TRY(check_weights(desc, w, true, true));
+  FLYAI_TRY(check_ep(desc, M, peers));
+  if (M > 0 && !x) return FLYAI_ERR_INVALID_ARG;
+  if (x && !aligned(x, 16)) return FLYAI_ERR_ALIGNMENT;
+  if (!tc_fused_supported(*desc, M, true)) return FLYAI_ERR_UNSUPPORTED;
+  const Workspace ws = carve_workspace(*desc, desc->max_tokens, workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const cudaEvent_t e0 = g_prof_start.load(), e1 = g_prof_stop.load();
+  if (e0 && e1 && cudaEventRecord(e0, s) != cudaSuccess) return FLYAI_ERR_CUDA;
+  FLYAI_TRY(launch_tc_forward(*desc, M, x, *w, nullptr, topk_ids, topk_weights, ws, s, peers));
+  if (e0 && e1 && cudaEventRecord(e1, s) != cudaSuccess) return FLYAI_ERR_CUDA;
+  return FLYAI_OK;
+}
+
 int flyai_moe_combine_ep(const flyai_moe_desc* desc, int32_t M, const flyai_moe_ep_peers* peers,
                          void* y, void* workspace, size_t workspace_bytes, void* stream) {
   FLYAI_TRY(check_desc(desc));

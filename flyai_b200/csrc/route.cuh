@@ -22,11 +22,14 @@ int launch_tc_experts(const flyai_moe_desc& d, int M, const void* x, bool x_spli
                       bool* folded = nullptr, const flyai_moe_ep_peers* ep = nullptr);
 // The whole verify-size layer in one launch (routing in the expert kernel's
 // prologue, the fold into y in its down epilogue): batches of 1..64 tokens with
-// at most 256 (token, slot) pairs on a GPU holding every expert.
-bool tc_fused_supported(const flyai_moe_desc& d, int M);
+// at most 256 (token, slot) pairs on a GPU holding every expert.  With ep, the
+// same launch for an expert shard: routing of every token over all experts,
+// this shard's experts, pair rows stored into every rank's mailbox and this
+// rank's flag raised (the fold is launch_combine_ep's).
+bool tc_fused_supported(const flyai_moe_desc& d, int M, bool ep = false);
 int launch_tc_forward(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_weights& w,
                       void* y, int32_t* ids_out, void* wts_out, const Workspace& ws,
-                      cudaStream_t stream);
+                      cudaStream_t stream, const flyai_moe_ep_peers* ep = nullptr);
 // Fold rows from this rank's mailbox once every rank's flag reached the epoch.
 int launch_combine_ep(const flyai_moe_desc& d, int M, const flyai_moe_ep_peers& ep, void* y,
                       const Workspace& ws, cudaStream_t stream);

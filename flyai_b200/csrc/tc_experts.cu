@@ -152,6 +152,7 @@ struct TcParams {
     const uint16_t* wr;
     const uint16_t* br;
     int M, E, k;
+    int e_begin, e_end;                     // this GPU's experts (expert parallel: a shard)
     float* logits;                          // [M, E] workspace
     int32_t* ids_ws;                        // [M*k] workspace copies of the routing
     float* wts_ws;
@@ -328,35 +329,39 @@ __device__ __forceinline__ void tc_route_logits(const TcParams::Route& r, int e,
 }
 
 // The plan of route_plan_small (route.cu) built by the whole CTA in shared
-// memory, one thread per (token, slot) pair p (P <= kTcThreads): p's place in
-// the stable permutation is (pairs of lower experts) + (earlier pairs of its own
+// memory, one thread per (token, slot) pair p (P <= kTcThreads), over the pairs
+// routed to this GPU's experts [e_begin, e_end): p's place in the stable
+// permutation is (local pairs of lower experts) + (earlier pairs of its own
 // expert); a pair whose rank inside its expert is a multiple of kTcChunk opens a
-// chunk, numbered after the chunks of the lower experts.  Two passes over the
-// P ids in shared memory, no serial scan over the experts.  Returns the number
-// of chunks; every thread of the CTA must call.
-__device__ __forceinline__ int tc_fused_plan(const int32_t* ids_s, int P, int32_t* perm_s,
-                                             int32_t* rin_s, int4* cinfo_s) {
+// chunk, numbered after the chunks of the lower experts.  Chunk descriptors
+// carry the local expert index (the bank holds the local experts only).  Two
+// passes over the P ids in shared memory, no serial scan over the experts.
+// Returns the number of chunks; every thread of the CTA must call.
+__device__ __forceinline__ int tc_fused_plan(const int32_t* ids_s, int P, int e_begin, int e_end,
+                                             int32_t* perm_s, int32_t* rin_s, int4* cinfo_s) {
   const int tid = threadIdx.x;
   int e = 0, less = 0, rin = 0, cnt = 0;
-  if (tid < P) {
+  const bool local = tid < P && ids_s[tid] >= e_begin && ids_s[tid] < e_end;
+  if (local) {
     e = ids_s[tid];
 #pragma unroll 4
     for (int q = 0; q < P; ++q) {
       const int eq = ids_s[q];
-      less += eq < e;
+      less += (eq < e) & (eq >= e_begin);
       rin += (eq == e) & (q < tid);
       cnt += eq == e;
     }
     perm_s[less + rin] = tid;
-    rin_s[tid] = rin;
   }
-  const bool opens = tid < P && rin % kTcChunk == 0;
+  if (tid < P) rin_s[tid] = local ? rin : 1;   // non-local pairs open nothing
+  const bool opens = local && rin % kTcChunk == 0;
   const int nch = __syncthreads_count(opens);
   if (opens) {
     int before = 0;
 #pragma unroll 4
-    for (int q = 0; q < P; ++q) before += (ids_s[q] < e) & (rin_s[q] % kTcChunk == 0);
-    cinfo_s[before + rin / kTcChunk] = make_int4(e, less + rin, min(kTcChunk, cnt - rin), 0);
+    for (int q = 0; q < P; ++q)
+      before += (ids_s[q] < e) & (ids_s[q] >= e_begin) & (rin_s[q] % kTcChunk == 0);
+    cinfo_s[before + rin / kTcChunk] = make_int4(e - e_begin, less + rin, min(kTcChunk, cnt - rin), 0);
   }
   return nch;
 }
@@ -462,7 +467,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
     if (threadIdx.x == 0) plan_words[2] = tc_grid_barrier(r.bar, gridDim.x);
     __syncthreads();
     if (!plan_words[2]) {   // the grid never met: nothing of this call is valid
-      if (threadIdx.x == 0) atomicOr(p.err, kErrWaitTimeout);
+      if (threadIdx.x == 0) {
+        tc_record_timeout(p);
+        if (p.ep_world) tc_ep_signal(p);   // peers see the failure word, not a silence
+      }
       if (warp == 1) tc::tmem_dealloc(tbase, 512);
       return;
     }
@@ -480,7 +488,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
     }
     __syncthreads();
     const int n_plan = tc_fused_plan(
-        ids_s, P, perm_s,
+        ids_s, P, r.e_begin, r.e_end, perm_s,
         reinterpret_cast<int32_t*>(tsm + static_cast<size_t>(kTcThreads / 32) * tc_topk_scratch(r.E)),
         cinfo_s);
     if (threadIdx.x < P) {   // slot order of each token by expert id (ids of a token differ)
@@ -792,7 +800,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
         }
       } else {
         tc_epilogue_down(p, val, ok ? nt : 0, pos0, t.mt, q, lane, bias_v, perm, wts);
-        if constexpr (kFused) {
+        if (kFused && p.ep_world == 0) {
           // a token whose k pair rows of this 128-column slice are now all stored
           // is folded into y here (the item's tokens are distinct)
           __threadfence();
@@ -1011,14 +1019,14 @@ int launch_tc_experts(const flyai_moe_desc& d, int M, const void* x, bool x_spli
   return FLYAI_OK;
 }
 
-bool tc_fused_supported(const flyai_moe_desc& d, int M) {
+bool tc_fused_supported(const flyai_moe_desc& d, int M, bool ep) {
   return M >= 1 && M < kTcPrefillMinTokens && M * d.top_k <= kTcFusedMaxPairs &&
-         d.expert_begin == 0 && d.expert_end == d.num_experts;
+         (ep || (d.expert_begin == 0 && d.expert_end == d.num_experts));
 }
 
 int launch_tc_forward(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_weights& w,
                       void* y, int32_t* ids_out, void* wts_out, const Workspace& ws,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, const flyai_moe_ep_peers* ep) {
   int dev = 0, sms = 0, max_smem = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -1045,6 +1053,8 @@ int launch_tc_forward(const flyai_moe_desc& d, int M, const void* x, const flyai
   r.M = M;
   r.E = d.num_experts;
   r.k = d.top_k;
+  r.e_begin = d.expert_begin;
+  r.e_end = d.expert_end;
   r.logits = ws.logits;
   r.ids_ws = ws.ids;
   r.wts_ws = ws.wts;
@@ -1054,6 +1064,18 @@ int launch_tc_forward(const flyai_moe_desc& d, int M, const void* x, const flyai
   r.fold_cnt = ws.fold_ticket;
   r.y = static_cast<uint16_t*>(y);
   r.clear_chunks = M * d.top_k < ws.max_chunks ? M * d.top_k : ws.max_chunks;
+  if (ep) {   // pair rows into every rank's mailbox, then this rank's flag (tc_ep_signal)
+    const size_t rows_bytes = static_cast<size_t>(d.max_tokens) * d.top_k * d.hidden * 2;
+    prm.ep_world = ep->world;
+    prm.ep_rank = ep->rank;
+    prm.ep_epoch = ep->epoch;
+    for (int i = 0; i < ep->world; ++i) {
+      uint8_t* mb = static_cast<uint8_t*>(ep->mailbox[i]);
+      prm.ep_flags[i] = reinterpret_cast<uint32_t*>(mb);
+      prm.ep_rows[i] = reinterpret_cast<uint16_t*>(mb + kEpFlagBytes + (ep->epoch & 1) * rows_bytes);
+    }
+    prm.ep_ticket = ws.route_ticket + kTicketEp;
+  }
 
   const size_t smem = tc_smem_layout(prm.kmax, prm.gu.L.tile_full, true).total;
   // prologue scratch in the weight ring: per warp E (value, index) pairs and E

@@ -12,14 +12,17 @@ rounding after every add -- the reference's own accumulation order
 (transformers/models/gpt_oss/modeling_gpt_oss.py:96-112).  The result is
 identical on every rank and identical to the single-GPU layer.
 
-Per step: broadcast x from the stage owner -> route (replicated, identical ids)
--> local experts -> exchange of the pair rows -> combine.  With ``p2p`` (the
-default on GPUs) the exchange is fused into the expert kernel: it stores each
-row straight into every rank's mailbox over NVLink (CUDA IPC mappings made once
-at set-up) and raises a per-rank flag; the combine waits for all flags.  The
-fallback, and the path of shapes the peer-memory kernel does not take, is an
-NCCL all-reduce of the rows.  Collectives run on torch.distributed (NCCL on
-GPUs, gloo in the CPU tests).
+Per step: route (replicated, identical ids) -> local experts -> exchange of the
+pair rows -> combine.  With ``broadcast`` (the default) x is meaningful on
+``src`` only -- the stage that owns the tokens -- and is broadcast first; with
+``broadcast=False`` every rank already holds the same x, as in the reference's
+pattern, and the step starts at the route.  With ``p2p`` (the default on GPUs) a verify-size call is
+one launch per rank (flyai_moe_forward_ep: the routing in the expert kernel's
+prologue, each pair row stored straight into every rank's mailbox over NVLink
+through CUDA IPC mappings made once at set-up, a per-rank flag raised at the
+end) and the combine waits for all flags.  The fallback, and the path of shapes
+the peer-memory kernel does not take, is an NCCL all-reduce of the rows.
+Collectives run on torch.distributed (NCCL on GPUs, gloo in the CPU tests).
 """
 import ctypes
 
@@ -93,22 +96,31 @@ class ExpertParallelMoE:
     shard that has ``experts_ep``) the pair-row exchange goes through peer
     memory, see the module docstring."""
 
-    def __init__(self, shard, group=None, src=0, p2p=True):
+    def __init__(self, shard, group=None, src=0, p2p=True, broadcast=True):
         import torch.distributed as dist
         self.dist = dist
         self.shard = shard
         self.group = group
         self.src = src
+        self.broadcast = broadcast
         self._pairs = None
         self.mail = None
         if p2p and hasattr(shard, "experts_ep") and dist.get_world_size(group) > 1:
             self.mail = PeerMailboxes(shard, group)
 
-    def forward(self, x, out=None):
-        """x: [M, H] bf16 (meaningful on ``src``; overwritten elsewhere) -> y on every rank."""
+    def forward(self, x, out=None, ids=None, wts=None):
+        """x: [M, H] bf16, the same on every rank (with ``broadcast``: meaningful on
+        ``src``, overwritten elsewhere) -> y on every rank.  ids / wts: optional
+        routing outputs of the one-launch path."""
         d = self.dist
-        d.broadcast(x, src=self.src, group=self.group)
+        if self.broadcast:
+            d.broadcast(x, src=self.src, group=self.group)
         M = x.shape[0]
+        if self.mail is not None and hasattr(self.shard, "forward_ep"):
+            peers = self.mail.next_epoch()
+            if self.shard.forward_ep(x, peers, ids, wts) == _lib.OK:
+                return self.shard.combine_ep(M, peers, out)
+            self.mail.peers.epoch -= 1   # shape without the one-launch path: same on every rank
         self.shard.route(x, logits=False)
         if self.mail is not None:
             peers = self.mail.next_epoch()

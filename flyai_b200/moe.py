@@ -193,6 +193,21 @@ class Mxfp4MoE:
             _lib.check("flyai_moe_experts_ep", st)
         return st
 
+    def forward_ep(self, x, peers, ids=None, wts=None):
+        """Expert parallel at verify size in one launch per rank (flyai_moe_forward_ep):
+        route every token over all experts, run this shard's experts, store their pair
+        rows into every rank's mailbox, raise this rank's flag.  x replicated on every
+        rank.  Optional outputs: ids int32 [M, k], wts bf16 [M, k].  Returns the status
+        code (``_lib.ERR_UNSUPPORTED`` for shapes without this path)."""
+        x = self._check_x(x)
+        st = _lib.load().flyai_moe_forward_ep(ctypes.byref(self.desc), x.shape[0], _ptr(x),
+                                              ctypes.byref(self.weights), ctypes.byref(peers),
+                                              _ptr(ids), _ptr(wts), _ptr(self.workspace),
+                                              self.workspace.numel(), _stream())
+        if st not in (_lib.OK, _lib.ERR_UNSUPPORTED):
+            _lib.check("flyai_moe_forward_ep", st)
+        return st
+
     def combine_ep(self, num_tokens, peers, out=None):
         """Wait for every rank's rows (bounded) and fold them: y bf16 [M, H]."""
         y = out if out is not None else torch.empty(num_tokens, self.hidden, dtype=torch.bfloat16, device=self.device)

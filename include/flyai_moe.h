@@ -302,6 +302,20 @@ FLYAI_API int flyai_moe_ipc_close(void* mailbox);
 FLYAI_API int flyai_moe_experts_ep(const flyai_moe_desc* desc, int32_t num_tokens, const void* x,
                                    const flyai_moe_weights* w, const flyai_moe_ep_peers* peers,
                                    void* workspace, size_t workspace_bytes, void* stream);
+/* Expert-parallel counterpart of flyai_moe_forward at verify sizes (1..64
+ * tokens, at most 256 pairs): ONE cooperative launch per rank routes every token
+ * over all experts (the same ids and weights on every rank), runs this rank's
+ * experts (desc's expert range) and stores their weighted pair rows into every
+ * rank's mailbox, then raises this rank's flag to `epoch` -- the routing and
+ * exchange of flyai_moe_route + flyai_moe_experts_ep in one kernel.  Tokens are
+ * replicated: every rank passes the same x, as in the reference's
+ * expert-sharded MoE (model.py:620-647).  Follow with flyai_moe_combine_ep.
+ * topk_ids / topk_weights (bf16) may be NULL.  Other shapes return
+ * FLYAI_ERR_UNSUPPORTED. */
+FLYAI_API int flyai_moe_forward_ep(const flyai_moe_desc* desc, int32_t num_tokens, const void* x,
+                                   const flyai_moe_weights* w, const flyai_moe_ep_peers* peers,
+                                   int32_t* topk_ids, void* topk_weights, void* workspace,
+                                   size_t workspace_bytes, void* stream);
 FLYAI_API int flyai_moe_combine_ep(const flyai_moe_desc* desc, int32_t num_tokens,
                                    const flyai_moe_ep_peers* peers, void* y, void* workspace,
                                    size_t workspace_bytes, void* stream);

@@ -106,6 +106,37 @@ def test_two_shards_in_one_process_reproduce_the_layer(layer):
             _lib.call("flyai_moe_ep_free", b)
 
 
+@pytest.mark.parametrize("M", [1, 5, 16])
+def test_one_launch_shards_reproduce_the_layer(layer, M):
+    """flyai_moe_forward_ep: each shard's single launch routes every token, runs its
+    own experts and stores their pair rows into both mailboxes; the combine then
+    equals the single-GPU layer bit for bit, and the routing outputs equal it too.
+    Both shards run in one process on one stream (rows and flags land before the
+    combine, so nothing waits on another launch)."""
+    E, H = layer.router_w.shape
+    x = synth.make_tokens(M, H, seed=11 + M).cuda()
+    shards = [Mxfp4MoE.from_layer(layer, expert_range=(r * E // 2, (r + 1) * E // 2), max_tokens=16,
+                                  device="cuda") for r in range(2)]
+    full = Mxfp4MoE.from_layer(layer, max_tokens=16, device="cuda")
+    y_full, ids_full, wts_full = full.forward(x)
+    boxes = _mailboxes(shards[0], 2)
+    try:
+        for epoch in (1, 2):                  # both mailbox halves (epoch parity)
+            ids = torch.empty_like(ids_full)
+            wts = torch.empty_like(wts_full)
+            for r in (1, 0):
+                assert shards[r].forward_ep(x, _peers(boxes, r, epoch), ids, wts) == _lib.OK
+            y = shards[0].combine_ep(M, _peers(boxes, 0, epoch))
+            torch.cuda.synchronize()
+            assert shards[0].read_error()[0] == 0 and shards[1].read_error()[0] == 0
+            assert torch.equal(y, y_full), epoch
+            assert torch.equal(ids, ids_full) and torch.equal(wts, wts_full)
+    finally:
+        torch.cuda.synchronize()
+        for b in boxes:
+            _lib.call("flyai_moe_ep_free", b)
+
+
 def test_combine_reports_a_rank_whose_expert_kernel_gave_up(layer):
     """A rank whose expert kernel gave up on a bounded wait raises its failure word
     to the epoch before its flag.  Here rank 1's flag and failure word are written
