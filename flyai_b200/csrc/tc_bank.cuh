@@ -167,21 +167,21 @@ struct TcStridedCursor {
   }
 };
 
-// Verify order: runs of kRun consecutive items (in chunk-major order) dealt
+// Verify order: runs of `run` consecutive items (in chunk-major order) dealt
 // round-robin -- CTA b takes runs b, b+G, ... of the gate/up items, then of
 // the down items.  A round covers a few whole chunks, so a chunk's gate/up tiles
 // finish together early in the phase and its down tiles, dealt later, find them
-// done; within a run the chunk (and its B operand) mostly stays the same.
-template <int kRun>
+// done; within a run the chunk (and its B operand) mostly stays the same.  With
+// few items per CTA a run of 1 spreads them over more SMs.
 struct TcRunCursor {
   TcItem t;
   long long u, n_gu, n_dn;   // item number within its phase; items per phase
-  int b, G, NI, NT;
-  __device__ __forceinline__ void start(int b_, int G_, long long nch, int NI_, int NT_) {
-    b = b_, G = G_, NI = NI_, NT = NT_;
+  int b, G, NI, NT, run;
+  __device__ __forceinline__ void start(int b_, int G_, long long nch, int NI_, int NT_, int run_) {
+    b = b_, G = G_, NI = NI_, NT = NT_, run = run_;
     n_gu = nch * NI, n_dn = nch * NT;
     t.gu = 1;
-    u = static_cast<long long>(b) * kRun;
+    u = static_cast<long long>(b) * run;
     if (u >= n_gu) t.gu = 0;   // no gate/up run for this CTA: its first down run
     set();
   }
@@ -195,14 +195,14 @@ struct TcRunCursor {
   // the item after v in this CTA's walk of the current phase: the next one of
   // the run, else the first of the CTA's next run
   __device__ __forceinline__ long long after(long long v) const {
-    return ((v + 1) % kRun != 0 && v + 1 < n_phase()) ? v + 1
-                                                       : v - v % kRun + static_cast<long long>(G) * kRun;
+    return ((v + 1) % run != 0 && v + 1 < n_phase()) ? v + 1
+                                                     : v - v % run + static_cast<long long>(G) * run;
   }
   __device__ __forceinline__ void next() {
     u = after(u);
     if (t.gu && u >= n_gu) {   // gate/up done: first down run of this CTA
       t.gu = 0;
-      u = static_cast<long long>(b) * kRun;
+      u = static_cast<long long>(b) * run;
     }
     if (valid()) set();
   }

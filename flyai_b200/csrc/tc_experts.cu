@@ -188,26 +188,32 @@ __device__ __forceinline__ void tc_record_timeout(const TcParams& p) {
 }
 
 // The last CTA of this rank's expert kernel raises this rank's flag to the
-// call's epoch in every rank's mailbox (system-scope release after every CTA's
-// rows were made visible system-wide).  When any CTA of the call gave up on a
-// wait it first raises this rank's failure word to the epoch, which the peers'
-// combine turns into an error instead of a fold.
+// call's epoch in every rank's mailbox.  Ordering: each CTA's peer row stores
+// reach its issuer through the epilogue's mbarrier arrive (release) and wait
+// (acquire); a GPU-scope fence orders them before the CTA's ticket; the last
+// CTA's ticket observes every other CTA's, and its system-scope fence, which is
+// cumulative over all of them, orders every row before the flag's system-scope
+// release -- one system fence per call, not one per CTA.  When any CTA of the
+// call gave up on a wait it first raises this rank's failure word to the epoch,
+// which the peers' combine turns into an error instead of a fold.
 __device__ __forceinline__ void tc_ep_signal(const TcParams& p) {
-  __threadfence_system();
+  __threadfence();
   if (atomicAdd(p.ep_ticket, 1) != static_cast<int>(gridDim.x) - 1) return;
   *p.ep_ticket = 0;
   __threadfence();
   const bool failed = atomicExch(p.ep_ticket + 1, 0) != 0;
+  // one system-scope fence, then relaxed system-scope stores: the fence makes
+  // each store a release (a release store per flag would fence once per rank)
   __threadfence_system();
-  for (int r = 0; r < p.ep_world; ++r) {
-    if (failed)
+  if (failed)
+    for (int r = 0; r < p.ep_world; ++r)
       asm volatile("st.relaxed.sys.global.u32 [%0], %1;\n" ::"l"(p.ep_flags[r] + kEpFailWord + p.ep_rank),
                    "r"(p.ep_epoch)
                    : "memory");
-    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p.ep_flags[r] + p.ep_rank),
-                 "r"(p.ep_epoch)
+  if (failed) __threadfence_system();   // the failure word lands before the flag
+  for (int r = 0; r < p.ep_world; ++r)
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;\n" ::"l"(p.ep_flags[r] + p.ep_rank), "r"(p.ep_epoch)
                  : "memory");
-  }
 }
 
 // Shared memory: weight ring, two B buffers (kTcChunk term rows each), one
@@ -521,9 +527,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
   }
   pdl_launch_dependents();
   const int mtg = p.gu.L.MT, mtd = p.dn.L.MT;
-  // Runs of kTcRun items dealt round-robin, gate/up then down (TcRunCursor).
-  TcRunCursor<kTcRun> cur;
-  cur.start(blockIdx.x, gridDim.x, nch, mtg, mtd);
+  // Runs of kTcRun items dealt round-robin, gate/up then down (TcRunCursor);
+  // runs of one when the gate/up items would not give every CTA a few runs.
+  TcRunCursor cur;
+  cur.start(blockIdx.x, gridDim.x, nch, mtg, mtd,
+            nch * mtg >= 4LL * gridDim.x ? kTcRun : 1);
   if (!cur.valid()) {   // nothing for this CTA
     if (warp == 1) tc::tmem_dealloc(tbase, 512);
     if (threadIdx.x == 0 && p.ep_world) tc_ep_signal(p);
@@ -704,7 +712,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
       const bool same_next = cur.next_same_b();
       int4 ci_next = ci;
       if (!same_next) {
-        TcRunCursor<kTcRun> nx = cur;
+        TcRunCursor nx = cur;
         nx.next();
         if (nx.valid()) ci_next = cinfo[nx.t.chunk];
       }
@@ -827,7 +835,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
       if (!same_next) chunk_items = 0;
       ci = ci_next;
     }
-    if (p.ep_world) __threadfence_system();   // peer row stores before the flag
     tc::fence_before_sync();
     __syncwarp();
     if (lane == 0) mbar_arrive(epi_done);
