@@ -33,6 +33,7 @@ MAX_TOKENS = 64
 
 _LOCK = threading.Lock()
 _INSTALLED = []   # modules whose MoE.forward this lever rebound
+_INSTALLED_DRAFTERS = []   # MoE instances bound by install_drafter
 _ATTEMPTS = [0]   # install() calls
 
 
@@ -171,6 +172,48 @@ def install(mod):
     return True
 
 
+def install_drafter(moes):
+    """Per-instance lever for the drafter's MoE blocks (the MTP blocks' ``MoE``
+    instances), as the reference binds its drafter lever after MTP construction
+    (engines/deepseek_v4/v4_dspark_moe.py:231-305, ``draft_forward``).  Each
+    instance's ``forward`` becomes the claimed path with the class's current
+    forward (the reference's, or ``install``'s) as its fallback; a drafter block
+    of T rows runs as one T-token layer call -- T x k (row, expert) pairs in one
+    launch chain, no host sync, routing and fold in the reference's order.
+    Unlike the reference's drafter lever it also claims T == 1 and hash-routed
+    blocks (one kernel path serves every T <= 64).  Returns how many instances
+    it bound; idempotent; a no-op with FLYAI_MOE_DEEPSEEK=0 or without CUDA."""
+    _ATTEMPTS[0] += 1
+    if not ENABLED or not torch.cuda.is_available():
+        return 0
+    bound = 0
+    for moe in moes:
+        if getattr(moe.__dict__.get("forward"), "_flyai_b200", False):
+            continue
+        prev = type(moe).forward
+        world = int(moe.__dict__.get("world_size", 1) or 1)
+
+        def forward(x, input_ids, _moe=moe, _prev=prev, _world=world):
+            return _claimed_forward(_moe, x, input_ids, _prev, _world)
+
+        forward._flyai_b200 = True
+        moe.forward = forward
+        bound += 1
+        with _LOCK:
+            _INSTALLED_DRAFTERS.append(moe)
+    return bound
+
+
+def uninstall_drafter(moes):
+    """Drop the per-instance forwards ``install_drafter`` bound."""
+    for moe in moes:
+        if getattr(moe.__dict__.get("forward"), "_flyai_b200", False):
+            del moe.forward
+        with _LOCK:
+            if moe in _INSTALLED_DRAFTERS:
+                _INSTALLED_DRAFTERS.remove(moe)
+
+
 def uninstall(mod):
     """Restore the forward that ``install`` replaced."""
     fwd = mod.MoE.forward
@@ -186,9 +229,11 @@ def attempts():
 
 
 def installed():
-    """Modules whose MoE.forward is this lever right now."""
+    """Modules whose MoE.forward is this lever right now, and drafter MoE
+    instances whose own forward is."""
     with _LOCK:
-        return [m for m in _INSTALLED if getattr(m.MoE.forward, "_flyai_b200", False)]
+        return ([m for m in _INSTALLED if getattr(m.MoE.forward, "_flyai_b200", False)] +
+                [m for m in _INSTALLED_DRAFTERS if getattr(m.__dict__.get("forward"), "_flyai_b200", False)])
 
 
 def coverage(module):

@@ -158,6 +158,36 @@ def test_deepseek_v4_lever_claims_decode_and_declines_prefill(monkeypatch):
     assert not getattr(mod.MoE.forward, "_flyai_b200", False)
 
 
+def test_deepseek_drafter_lever_binds_instances(monkeypatch):
+    """install_drafter: the drafter's MoE instances (a T-row block: T x k pairs)
+    run on the kernels while other instances of the class keep the reference's
+    forward; the result equals the oracle, the class is untouched."""
+    monkeypatch.setattr(deepseek, "ENABLED", True)
+    mod, calls = _reference_module()
+    layer = synth.make_v4_layer(num_experts=32, top_k=6, hidden=256, inter=256, seed=53)
+    drafter, main = _v4_block(mod, layer, 0), _v4_block(mod, layer, 1)
+    assert deepseek.install_drafter([drafter]) == 1
+    assert deepseek.install_drafter([drafter]) == 0            # idempotent
+    assert not getattr(mod.MoE.forward, "_flyai_b200", False)  # the class is not rebound
+    T = 5                                                       # a drafter block: 5 rows x 6 experts
+    x = synth.make_tokens(T, 256, seed=70, device="cuda")
+    ii = torch.zeros(1, T, dtype=torch.long, device="cuda")
+    y = drafter(x.view(1, T, 256), ii)
+    torch.cuda.synchronize()
+    xc = x.float().cpu().numpy()
+    ids, wts, _ = ov4.gate(xc, layer.router_w.float().numpy(), layer.bias.numpy(), 6, layer.route_scale)
+    y_ref = ov4.moe_forward(xc, ids, wts, expert_np(layer), shared_np(layer), layer.swiglu_limit)
+    assert_close(y.view(T, 256).float().cpu().numpy(), y_ref)
+    main(x.view(1, T, 256), ii)                                 # the reference's forward
+    assert calls == [(1, T, 256)]
+    assert deepseek.coverage(drafter)[0] == (1, {})
+    assert drafter in deepseek.installed()
+    deepseek.uninstall_drafter([drafter])
+    assert drafter not in deepseek.installed()
+    drafter(x.view(1, T, 256), ii)
+    assert len(calls) == 2
+
+
 def test_deepseek_v3_lever_on_fp8_block_with_grouped_gate(monkeypatch):
     monkeypatch.setattr(deepseek, "ENABLED", True)
     mod, calls = _reference_module()
