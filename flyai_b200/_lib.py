@@ -41,7 +41,7 @@ EXPORTS = (
     "flyai_moe_ep_free", "flyai_moe_ipc_get_handle", "flyai_moe_ipc_open", "flyai_moe_ipc_close",
     "flyai_moe_experts_ep", "flyai_moe_combine_ep", "flyai_moe_forward_ep",
     "flyai_moe_forward_noalloc", "flyai_moe_read_error", "flyai_moe_pack_fp8",
-    "flyai_moe_pack_nvfp4", "flyai_moe_pack_fp4", "flyai_moe_pack_shared_fp8",
+    "flyai_moe_pack_nvfp4", "flyai_moe_pack_nvfp4_swizzled", "flyai_moe_pack_fp4", "flyai_moe_pack_shared_fp8",
     "flyai_moe_route_hash", "flyai_moe_route_logits",
 )
 
@@ -81,6 +81,29 @@ class FlyaiError(RuntimeError):
         self.status = status
 
 
+class FlyaiDeviceError(RuntimeError):
+    """A kernel of a call gave up on a bounded wait and set the workspace's
+    error word: that call's output is not valid (it is zero, or partial)."""
+
+
+# FLYAI_MOE_CHECK=1: every layer call reads the workspace error word back and
+# raises FlyaiDeviceError when it is set.  The read synchronises the host with
+# the stream, so it is off by default and skipped while a CUDA graph is captured.
+CHECK = os.environ.get("FLYAI_MOE_CHECK", "0") not in ("", "0")
+
+
+def checking():
+    """FLYAI_MOE_CHECK is on and the current stream is not capturing."""
+    import torch
+    return CHECK and not torch.cuda.is_current_stream_capturing()
+
+
+def raise_on_error_bits(bits, where):
+    if bits:
+        raise FlyaiDeviceError(f"{where}: a kernel gave up on a bounded wait (error bits {bits:#x}); "
+                               "the output of this call is not valid")
+
+
 _lib = None
 
 
@@ -102,6 +125,7 @@ def load():
         "flyai_moe_pack_mxfp4": ([pd, i32, vp, vp, vp, vp], ctypes.c_int),
         "flyai_moe_pack_fp8": ([pd, i32, vp, vp, vp, vp], ctypes.c_int),
         "flyai_moe_pack_nvfp4": ([pd, i32, vp, vp, vp, vp, vp], ctypes.c_int),
+        "flyai_moe_pack_nvfp4_swizzled": ([pd, i32, vp, vp, vp, vp, vp], ctypes.c_int),
         "flyai_moe_pack_fp4": ([pd, i32, vp, vp, vp, vp], ctypes.c_int),
         "flyai_moe_pack_shared_fp8": ([pd, i32, vp, vp, vp, vp], ctypes.c_int),
         "flyai_moe_route_hash": ([pd, i32, vp, vp, vp, i32, pw, vp, vp, vp, vp, sz, vp], ctypes.c_int),

@@ -257,8 +257,8 @@ int flyai_moe_pack_shared_fp8(const flyai_moe_desc* desc, int32_t proj, const vo
   return launch_v4_pack_shared(*desc, proj, weight, scale, packed, static_cast<cudaStream_t>(stream));
 }
 
-int flyai_moe_pack_nvfp4(const flyai_moe_desc* desc, int32_t proj, const void* blocks,
-                         const void* scales, const void* global_scale, void* packed, void* stream) {
+static int pack_nvfp4(const flyai_moe_desc* desc, int32_t proj, const void* blocks, const void* scales,
+                      const void* global_scale, void* packed, void* stream, bool swizzled) {
   FLYAI_TRY(check_desc(desc));
   if (proj != FLYAI_PROJ_W13 && proj != FLYAI_PROJ_W2) return FLYAI_ERR_INVALID_ARG;
   if (desc->format != FLYAI_FMT_NVFP4) return FLYAI_ERR_UNSUPPORTED;
@@ -267,7 +267,18 @@ int flyai_moe_pack_nvfp4(const flyai_moe_desc* desc, int32_t proj, const void* b
   if (!aligned(blocks, 16) || !aligned(packed, 16) || !aligned(global_scale, 4))
     return FLYAI_ERR_ALIGNMENT;
   return launch_nv4_pack(*desc, proj, blocks, scales, global_scale, packed,
-                         static_cast<cudaStream_t>(stream));
+                         static_cast<cudaStream_t>(stream), swizzled);
+}
+
+int flyai_moe_pack_nvfp4(const flyai_moe_desc* desc, int32_t proj, const void* blocks,
+                         const void* scales, const void* global_scale, void* packed, void* stream) {
+  return pack_nvfp4(desc, proj, blocks, scales, global_scale, packed, stream, false);
+}
+
+int flyai_moe_pack_nvfp4_swizzled(const flyai_moe_desc* desc, int32_t proj, const void* blocks,
+                                  const void* scales, const void* global_scale, void* packed,
+                                  void* stream) {
+  return pack_nvfp4(desc, proj, blocks, scales, global_scale, packed, stream, true);
 }
 
 int flyai_moe_workspace_bytes(const flyai_moe_desc* desc, size_t* bytes) {

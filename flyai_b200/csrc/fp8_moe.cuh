@@ -173,7 +173,7 @@ int launch_fp8_route(const flyai_moe_desc& d, int M, const void* x, const flyai_
                      const void* logits_in = nullptr);
 size_t nv4_packed_bytes(const flyai_moe_desc& d, int proj);
 int launch_nv4_pack(const flyai_moe_desc& d, int proj, const void* blocks, const void* scales,
-                    const void* global_scale, void* packed, cudaStream_t stream);
+                    const void* global_scale, void* packed, cudaStream_t stream, bool swizzled = false);
 // Expert projections on the plan flyai_moe_route left in ws: this shard's rows
 // (by flat pair index, the shared expert's after the M*k pairs) into `rows`,
 // then, when y is not null, the fold of all rows into y.

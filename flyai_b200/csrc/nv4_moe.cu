@@ -60,8 +60,14 @@ size_t nv4_packed_bytes(const flyai_moe_desc& d, int proj) {
 // One thread per 16-byte unit of a tile: data units c*128 + r (K-chunk c of row
 // r, canonical K-major position), then the two scale chunks (32 lines each;
 // line l holds rows l, l+32, l+64, l+96, four block-16 scales apiece).
+// Scales come linear ([R, K/16] per expert) or, with swz, in the block-scale
+// layout of the CUTLASS / FlashInfer NVFP4 kernels that vLLM swizzles a loaded
+// layer's scales into (vllm/model_executor/layers/quantization/utils/
+// nvfp4_utils.py swizzle_blockscale): per expert the [R, C = K/16] matrix padded
+// to [roundup(R, 128), roundup(C, 4)], element (r, c) at
+// ((r / 128 * (C' / 4) + c / 4) * 32 + r % 32) * 16 + (r % 128) / 32 * 4 + c % 4.
 __global__ void nv4_pack_kernel(const uint8_t* __restrict__ blocks, const uint8_t* __restrict__ scales,
-                                uint8_t* __restrict__ packed, int nexp, int R, int K, NvBank b) {
+                                uint8_t* __restrict__ packed, int nexp, int R, int K, NvBank b, int swz) {
   constexpr int kUnits = kNvTileBytes / 16;   // 576
   const size_t total = static_cast<size_t>(nexp) * b.RB * b.KB * b.tiles * kUnits;
   const int half_rows = b.tiles == 2 ? R / 2 : 0;
@@ -81,10 +87,16 @@ __global__ void nv4_pack_kernel(const uint8_t* __restrict__ blocks, const uint8_
       out = *reinterpret_cast<const uint4*>(blocks + (row0 + r) * (K / 2) + kb * 64 + c * 16);
     } else {
       const int w = v - kNvTile / 16, j = w / 32, l = w % 32;
+      const int C = K / 16, c0 = kb * 8 + j * 4;
+      const size_t Rp = (static_cast<size_t>(R) + 127) / 128 * 128, Cp = (static_cast<size_t>(C) + 3) / 4 * 4;
       uint32_t word[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const uint8_t* s = scales + (row0 + 32 * q + l) * (K / 16) + kb * 8 + j * 4;
+        const size_t rl = static_cast<size_t>(tt) * half_rows + rb * 128 + 32 * q + l;   // row in the expert
+        const uint8_t* s =
+            swz ? scales + static_cast<size_t>(e) * Rp * Cp +
+                      ((rl / 128 * (Cp / 4) + c0 / 4) * 32 + rl % 32) * 16 + (rl % 128) / 32 * 4
+                : scales + (row0 + 32 * q + l) * C + c0;
         word[q] = static_cast<uint32_t>(s[0]) | (static_cast<uint32_t>(s[1]) << 8) |
                   (static_cast<uint32_t>(s[2]) << 16) | (static_cast<uint32_t>(s[3]) << 24);
       }
@@ -96,7 +108,7 @@ __global__ void nv4_pack_kernel(const uint8_t* __restrict__ blocks, const uint8_
 }
 
 int launch_nv4_pack(const flyai_moe_desc& d, int proj, const void* blocks, const void* scales,
-                    const void* global_scale, void* packed, cudaStream_t stream) {
+                    const void* global_scale, void* packed, cudaStream_t stream, bool swizzled) {
   const int nexp = d.expert_end - d.expert_begin + d.n_shared;
   if (nexp == 0) return FLYAI_OK;
   const NvBank b = nv_bank(d.hidden, d.inter, proj);
@@ -104,7 +116,7 @@ int launch_nv4_pack(const flyai_moe_desc& d, int proj, const void* blocks, const
   const int K = proj == FLYAI_PROJ_W13 ? d.hidden : d.inter;
   nv4_pack_kernel<<<2368, 256, 0, stream>>>(static_cast<const uint8_t*>(blocks),
                                             static_cast<const uint8_t*>(scales),
-                                            static_cast<uint8_t*>(packed), nexp, R, K, b);
+                                            static_cast<uint8_t*>(packed), nexp, R, K, b, swizzled ? 1 : 0);
   note_launch();
   if (cudaGetLastError() != cudaSuccess) return FLYAI_ERR_CUDA;
   if (cudaMemcpyAsync(static_cast<uint8_t*>(packed) + nv_global_offset(d, proj), global_scale,

@@ -188,9 +188,16 @@ class Fp8MoE:
             _lib.call("flyai_moe_forward", ctypes.byref(self.desc), M, _ptr(x),
                       ctypes.byref(self.weights), _ptr(y), _ptr(ids), _ptr(wts),
                       _ptr(self.workspace), self.workspace.numel(), _stream())
+        if _lib.checking():
+            self.raise_on_error(type(self).__name__ + ".forward")
         return y
 
     __call__ = forward
+
+    def raise_on_error(self, where=None):
+        """Raise FlyaiDeviceError if a kernel left the error word set (reads and
+        clears it; synchronises the host with the stream)."""
+        _lib.raise_on_error_bits(self.read_error(clear=True)[0], where or type(self).__name__)
 
     def read_error(self, clear=True):
         out = torch.zeros(9, dtype=torch.int32, device=self.device)

@@ -30,10 +30,14 @@ class Nvfp4MoE(Fp8MoE):
     experts, bf16 fold in ascending expert id."""
 
     def __init__(self, router_w, bias, expert, num_experts, hidden, inter, top_k,
-                 route_scale=1.0, max_tokens=64, device=None, experts=None, expert_range=None):
+                 route_scale=1.0, max_tokens=64, device=None, experts=None, expert_range=None,
+                 scales_swizzled=False):
         """``expert(e)`` -> (w13 uint8 [2I, H/2] = [w1; w3] packed nibbles, s13 e4m3
         [2I, H/16], g13 fp32 [2] (w1's, w3's weight_scale_2), w2 uint8 [H, I/2], s2 e4m3
-        [H, I/16], g2 fp32 [1]) -- the ModelOpt NVFP4 tensors of one expert.
+        [H, I/16], g2 fp32 [1]) -- the ModelOpt NVFP4 tensors of one expert; with
+        ``scales_swizzled`` s13 / s2 come in the block-scale layout vLLM swizzles a
+        loaded layer's scales into (flyai_moe_pack_nvfp4_swizzled), as they are read
+        from a FusedMoE layer after loading.
         ``expert_range`` = (lo, hi) makes an expert-parallel shard (see Fp8MoE)."""
         _lib.load()
         device = torch.device(device or router_w.device)
@@ -47,6 +51,7 @@ class Nvfp4MoE(Fp8MoE):
         self.num_experts, self.hidden, self.inter, self.top_k = E, H, I, top_k
         self.n_shared = 0
         self.expert_range = (lo, hi)
+        self.scales_swizzled = scales_swizzled
         self.desc = _lib.Desc(
             abi_version=_lib.ABI_VERSION, format=_lib.FMT_NVFP4, gating=_lib.GATE_SIGMOID_BF16,
             activation=_lib.ACT_SILU_BF16, num_experts=E, top_k=top_k, hidden=H, inter=I,
@@ -89,8 +94,8 @@ class Nvfp4MoE(Fp8MoE):
         g = gscale.to(device=self.device, dtype=torch.float32).contiguous()
         stage = torch.empty(per.value, dtype=torch.uint8, device=self.device)
         with torch.cuda.device(self.device):
-            _lib.call("flyai_moe_pack_nvfp4", ctypes.byref(d), proj, _ptr(blocks), _ptr(scales),
-                      _ptr(g), _ptr(stage), _stream())
+            _lib.call("flyai_moe_pack_nvfp4_swizzled" if self.scales_swizzled else "flyai_moe_pack_nvfp4",
+                      ctypes.byref(d), proj, _ptr(blocks), _ptr(scales), _ptr(g), _ptr(stage), _stream())
         ng = 2 if proj == _lib.PROJ_W13 else 1
         expert_bytes = self._expert_bytes(proj)
         if per.value != (expert_bytes + ng * 4 + 255) // 256 * 256:

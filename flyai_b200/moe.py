@@ -156,7 +156,14 @@ class Mxfp4MoE:
         _lib.call("flyai_moe_forward", ctypes.byref(self.desc), M, _ptr(x), ctypes.byref(self.weights),
                   _ptr(y), _ptr(ids), _ptr(wts), _ptr(self.workspace),
                   self.workspace.numel(), _stream())
+        if _lib.checking():
+            self.raise_on_error("Mxfp4MoE.forward")
         return y, ids, wts
+
+    def raise_on_error(self, where="Mxfp4MoE"):
+        """Raise FlyaiDeviceError if a kernel left the error word set (reads and
+        clears it; synchronises the host with the stream)."""
+        _lib.raise_on_error_bits(self.read_error(clear=True)[0], where)
 
     def experts(self, x, out=None):
         """Experts + combine on the routing of the last ``route(x)`` (same stream)."""
@@ -213,6 +220,8 @@ class Mxfp4MoE:
         y = out if out is not None else torch.empty(num_tokens, self.hidden, dtype=torch.bfloat16, device=self.device)
         _lib.call("flyai_moe_combine_ep", ctypes.byref(self.desc), num_tokens, ctypes.byref(peers),
                   _ptr(y), _ptr(self.workspace), self.workspace.numel(), _stream())
+        if _lib.checking():
+            self.raise_on_error("Mxfp4MoE.combine_ep")
         return y
 
     def combine(self, pair_out, num_tokens, out=None):

@@ -167,6 +167,14 @@ FLYAI_API int flyai_moe_pack_fp8(const flyai_moe_desc* desc, int32_t proj, const
 FLYAI_API int flyai_moe_pack_nvfp4(const flyai_moe_desc* desc, int32_t proj, const void* blocks,
                                    const void* scales, const void* global_scale, void* packed,
                                    void* stream);
+/* Same, with the scales in the block-scale layout vLLM swizzles a loaded NVFP4
+ * layer into for the CUTLASS / FlashInfer kernels (vllm/model_executor/layers/
+ * quantization/utils/nvfp4_utils.py swizzle_blockscale): per expert the [R, K/16]
+ * matrix padded to [roundup(R, 128), roundup(K/16, 4)] and stored as
+ * [R'/128][C'/4][32][4][4] -- for banks taken from a layer vLLM already loaded. */
+FLYAI_API int flyai_moe_pack_nvfp4_swizzled(const flyai_moe_desc* desc, int32_t proj, const void* blocks,
+                                            const void* scales, const void* global_scale, void* packed,
+                                            void* stream);
 
 /* Load-time relayout of DeepSeek-V4 fp4 routed experts into the kernel bank
  * (FLYAI_FMT_FP4_W4A8).  blocks: uint8 [El, R, K/2] packed e2m1 (the checkpoint's

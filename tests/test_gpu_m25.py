@@ -268,3 +268,35 @@ def test_cuda_graph_replay_matches_eager(M):
     torch.cuda.synchronize()
     assert torch.equal(static_y, y_eager)
     assert moe.read_error()[0] == 0
+
+
+def _swizzle_blockscale(s):
+    """vLLM's block-scale swizzle of a [R, C] e4m3 scale matrix
+    (vllm/model_executor/layers/quantization/utils/nvfp4_utils.py): padded to
+    [roundup(R, 128), roundup(C, 4)], reshaped [R'/128, 4, 32, C'/4, 4] and
+    permuted to [R'/128, C'/4, 32, 4, 4]."""
+    u = s.contiguous().view(torch.uint8)
+    R, C = u.shape
+    Rp, Cp = (R + 127) // 128 * 128, (C + 3) // 4 * 4
+    pad = torch.zeros(Rp, Cp, dtype=torch.uint8, device=u.device)
+    pad[:R, :C] = u
+    return pad.reshape(Rp // 128, 4, 32, Cp // 4, 4).permute(0, 3, 2, 1, 4).contiguous().reshape(Rp, Cp)
+
+
+def test_swizzled_scales_pack_to_the_same_bank():
+    """flyai_moe_pack_nvfp4_swizzled on vLLM-swizzled scales writes the bank the
+    linear-scale pack writes, and the layer computes the same output."""
+    layer = synth.make_m25_layer(num_experts=32, top_k=4, hidden=256, inter=128, seed=17)
+
+    def expert_swz(e):
+        w13, s13, g13, w2, s2, g2 = layer.expert(e)
+        return w13, _swizzle_blockscale(s13), g13, w2, _swizzle_blockscale(s2), g2
+
+    lin = Nvfp4MoE.from_layer(layer, max_tokens=8, device="cuda")
+    swz = Nvfp4MoE(layer.router_w, layer.bias, expert_swz, layer.num_experts, layer.hidden, layer.inter,
+                   layer.top_k, route_scale=layer.route_scale, max_tokens=8, device="cuda",
+                   scales_swizzled=True)
+    torch.cuda.synchronize()
+    assert torch.equal(lin.w13, swz.w13) and torch.equal(lin.w2, swz.w2)
+    x = synth.make_tokens(5, 256, seed=18).cuda()
+    assert torch.equal(lin.forward(x), swz.forward(x))
