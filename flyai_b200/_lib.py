@@ -95,7 +95,9 @@ CHECK = os.environ.get("FLYAI_MOE_CHECK", "0") not in ("", "0")
 def checking():
     """FLYAI_MOE_CHECK is on and the current stream is not capturing."""
     import torch
-    return CHECK and not torch.cuda.is_current_stream_capturing()
+    if not CHECK:
+        return False
+    return not (torch.cuda.is_available() and torch.cuda.is_current_stream_capturing())
 
 
 def raise_on_error_bits(bits, where):
