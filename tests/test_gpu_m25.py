@@ -297,6 +297,10 @@ def test_swizzled_scales_pack_to_the_same_bank():
                    layer.top_k, route_scale=layer.route_scale, max_tokens=8, device="cuda",
                    scales_swizzled=True)
     torch.cuda.synchronize()
-    assert torch.equal(lin.w13, swz.w13) and torch.equal(lin.w2, swz.w2)
+    from flyai_b200 import _lib
+    E = layer.num_experts
+    for proj, a, b, ng in ((_lib.PROJ_W13, lin.w13, swz.w13, 2), (_lib.PROJ_W2, lin.w2, swz.w2, 1)):
+        used = E * lin._expert_bytes(proj) + E * ng * 4   # tiles, then the global scales (rest: padding)
+        assert torch.equal(a[:used], b[:used]), proj
     x = synth.make_tokens(5, 256, seed=18).cuda()
     assert torch.equal(lin.forward(x), swz.forward(x))
