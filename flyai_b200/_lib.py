@@ -31,6 +31,10 @@ ACT_SILU = 2
 ACT_SILU_BF16 = 3
 PROJ_W13 = 0
 PROJ_W2 = 1
+LIN_SCALE_F32 = 0
+LIN_SCALE_E8M0 = 1
+LIN_FMT_AMAX = 0
+LIN_FMT_UE8M0 = 1
 
 EXPORTS = (
     "flyai_moe_abi_version", "flyai_moe_strerror", "flyai_moe_check_desc",
@@ -43,6 +47,8 @@ EXPORTS = (
     "flyai_moe_forward_noalloc", "flyai_moe_read_error", "flyai_moe_pack_fp8",
     "flyai_moe_pack_nvfp4", "flyai_moe_pack_nvfp4_swizzled", "flyai_moe_pack_fp4", "flyai_moe_pack_shared_fp8",
     "flyai_moe_route_hash", "flyai_moe_route_logits",
+    "flyai_fp8_linear_bank_bytes", "flyai_fp8_linear_pack", "flyai_fp8_linear_workspace_bytes",
+    "flyai_fp8_linear",
 )
 
 
@@ -152,6 +158,10 @@ def load():
         "flyai_moe_read_plan": ([pd, i32, vp, sz, vp, vp, vp, vp], ctypes.c_int),
         "flyai_moe_forward_noalloc": ([pd, i32, vp, pw, vp, vp, vp, vp], ctypes.c_int),
         "flyai_moe_read_error": ([pd, vp, sz, vp, i32, vp], ctypes.c_int),
+        "flyai_fp8_linear_bank_bytes": ([i32, i32, ctypes.POINTER(sz)], ctypes.c_int),
+        "flyai_fp8_linear_pack": ([i32, i32, vp, vp, i32, vp, vp], ctypes.c_int),
+        "flyai_fp8_linear_workspace_bytes": ([i32, i32, i32, ctypes.POINTER(sz)], ctypes.c_int),
+        "flyai_fp8_linear": ([i32, i32, i32, vp, vp, i32, vp, vp, sz, vp], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)

@@ -14,8 +14,9 @@ CSRC = os.path.join(HERE, "csrc")
 OUT_DIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(OUT_DIR, "libflyai_moe.so")
 SOURCES = ["abi.cu", "route.cu", "combine.cu", "tc_experts.cu", "tc_prefill.cu", "fp8_moe.cu", "nv4_moe.cu", "nv4_prefill.cu", "v4_moe.cu",
+           "fp8_linear.cu",
            "noalloc.cu"]
-HEADERS = ["common.cuh", "route.cuh", "route_dev.cuh", "torch_topk.cuh", "tcgen05.cuh", "terms.cuh", "tc_bank.cuh", "fp8_moe.cuh", "nv4.cuh", "v4.cuh"]
+HEADERS = ["act_quant.cuh", "common.cuh", "route.cuh", "route_dev.cuh", "torch_topk.cuh", "tcgen05.cuh", "terms.cuh", "tc_bank.cuh", "fp8_moe.cuh", "nv4.cuh", "v4.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -26,6 +26,7 @@
 
 #include <type_traits>
 
+#include "act_quant.cuh"
 #include "common.cuh"
 #include "fp8_moe.cuh"
 #include "tc_bank.cuh"
@@ -34,14 +35,6 @@
 #include "v4.cuh"
 
 namespace flyai {
-
-// fp32 1/448 as torch forms it for `amax * (1.0 / FP8_MAX)` on an fp32 tensor.
-__device__ __constant__ float kF8Inv448 = static_cast<float>(1.0 / 448.0);
-
-__device__ __forceinline__ uint32_t f32_to_e4m3(float v) {
-  v = fminf(fmaxf(v, -448.f), 448.f);
-  return static_cast<uint32_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
-}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -252,15 +245,8 @@ __device__ int f8_block_scan(int v, int* tmp, int* total) {
 // ue8m0: the scale is 2^ceil(log2(amax/448)) (scale_fmt "ue8m0"), else amax/448.
 __device__ __forceinline__ void f8_quant_block(const uint16_t* src, uint8_t* q, float* sc, int lane,
                                                int ue8m0) {
-  const uint2 raw = __ldg(reinterpret_cast<const uint2*>(src + lane * 4));
-  const float v[4] = {__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xFFFF0000u),
-                      __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xFFFF0000u)};
-  float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-  a = fmaxf(warp_max(a), 1e-4f);
-  const float s = ue8m0 ? exp2_int(ue8m0_exp(a, kF8Inv448)) : __fmul_rn(a, kF8Inv448);
-  uint32_t packed = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) packed |= f32_to_e4m3(__fdiv_rn(v[j], s)) << (8 * j);
+  float s;
+  const uint32_t packed = act_quant4(src, lane, ue8m0, s);
   *reinterpret_cast<uint32_t*>(q + lane * 4) = packed;
   if (lane == 0) *sc = s;
 }

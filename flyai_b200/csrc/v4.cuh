@@ -7,6 +7,7 @@
 // (dtype "fp8", scale_dtype "fp8").  Activations are e4m3 with one power-of-two
 // scale per 1x128 block (act_quant with scale_fmt "ue8m0").
 #pragma once
+#include "act_quant.cuh"
 #include "common.cuh"
 #include "fp8_moe.cuh"
 
@@ -56,17 +57,6 @@ __host__ __device__ inline V4Bank v4_bank(const flyai_moe_desc& d, int proj) {
 }
 
 __host__ __device__ inline bool is_v4(const flyai_moe_desc& d) { return d.format == FLYAI_FMT_FP4_W4A8; }
-
-// The ue8m0 activation scale of a 128-block with maximum |x| = amax:
-// 2^ceil(log2(max(amax, 1e-4) * (1/448))), exact at powers of two (the
-// reference's fast_round_scale, engines/deepseek_v4/v4_kernels_cpu.py:68-76).
-// Returns the exponent; the scale is 2^exponent.
-__device__ __forceinline__ int ue8m0_exp(float amax, float inv448) {
-  const uint32_t b = __float_as_uint(__fmul_rn(fmaxf(amax, 1e-4f), inv448));
-  const int e = static_cast<int>((b >> 23) & 0xFFu) - 127;
-  return e + ((b & 0x7FFFFFu) != 0u ? 1 : 0);
-}
-__device__ __forceinline__ float exp2_int(int e) { return __uint_as_float(static_cast<uint32_t>(e + 127) << 23); }
 
 // e2m1 nibbles -> e4m3 bytes, exact (every e2m1 value is an e4m3 value): the 8
 // packed elements of w (low nibble first) become the 8 bytes of (lo, hi).  The

@@ -37,6 +37,12 @@ M25 = dict(num_experts=256, top_k=8, hidden=3072, inter=1536)
 # dim 4096, moe_inter_dim 2048, 256 routed experts (fp4), 6 active, 1 shared
 # expert (fp8), sqrtsoftplus scores, route_scale 1.5, swiglu_limit 10.
 V4 = dict(num_experts=256, top_k=6, hidden=4096, inter=2048, route_scale=1.5, swiglu_limit=10.0)
+# The fp8 weights [N, K] a DeepSeek-V4-Flash decode layer multiplies one token
+# row by (engines/deepseek_v4/v4_fp8_gemv.py:10-14): attention, the ratio-4
+# layers' indexer wq_b, and the shared expert (w1 and w3 read the same x).
+V4_LINEARS = dict(wq_a=(1024, 4096), wkv=(512, 4096), wo_b=(4096, 8192), wq_b=(32768, 1024),
+                  idx_wq_b=(8192, 1024), shared_w1=(2048, 4096), shared_w3=(2048, 4096),
+                  shared_w2=(4096, 2048))
 
 
 @dataclass
@@ -261,3 +267,17 @@ def make_v4_layer(num_experts, top_k, hidden, inter, route_scale=1.5, swiglu_lim
         tid2eid = torch.randint(0, num_experts, (hash_vocab, top_k), dtype=torch.int32, **rnd)
     return V4Layer(router_w, bias, inter, top_k, route_scale, swiglu_limit, seed, tid2eid,
                    str(device))
+
+
+def make_fp8_linear(N, K, seed=0, e8m0=True, device="cpu"):
+    """An fp8 Linear's (weight e4m3 [N, K] from N(0, 1), scale [N/128, K/128]):
+    e8m0 bytes uniform in [117, 120] (a "scale_dtype fp8" checkpoint, as the V4
+    shared expert), else fp32 lognormal(-6, 0.5) as the DeepSeek-V3 experts."""
+    g = torch.Generator(device=device).manual_seed(seed * 1_000_003 + 7919 * N + K)
+    rnd = dict(generator=g, device=device)
+    w = torch.randn(N, K, **rnd).to(torch.float8_e4m3fn)
+    if e8m0:
+        s = torch.randint(117, 121, (N // 128, K // 128), dtype=torch.uint8, **rnd)
+    else:
+        s = torch.exp(torch.randn(N // 128, K // 128, **rnd) * 0.5 - 6.0)
+    return w, s

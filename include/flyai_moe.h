@@ -373,6 +373,39 @@ FLYAI_API int64_t flyai_moe_launch_count(void);
  * can time the dominant kernel alone.  Pass nulls to switch it off. */
 FLYAI_API int flyai_moe_set_profile_events(void* start, void* stop);
 
+/* ---- Dense FP8 linear ----------------------------------------------------------
+ * y = linear(x, W) for an e4m3 weight W [N, K] with one scale per 128x128 block
+ * (vendor/deepseek_v4_ref/inference/model.py:114-124 `linear` on a float8_e4m3fn
+ * weight: act_quant of x per 1x128, then fp8_gemm, kernel.py:203-274), at the
+ * decode / verify sizes the reference's GEMV lever serves
+ * (engines/deepseek_v4/v4_fp8_gemv.py:178-262 fp8_gemm_tiled_kernel and its
+ * dispatch).  x bf16 [M, K], y bf16 [M, N]; N and K multiples of 128.
+ * Per element: acc = D_kb * (s_x * s_w) + acc in fp32 over ascending 128-wide K
+ * blocks (D_kb the block's e4m3 dot product), rounded once to bf16. */
+#define FLYAI_LIN_SCALE_F32   0  /* weight scales fp32 [N/128, K/128]                          */
+#define FLYAI_LIN_SCALE_E8M0  1  /* weight scales e8m0 bytes [N/128, K/128] (float8_e8m0fnu)   */
+#define FLYAI_LIN_FMT_AMAX    0  /* activation scale amax/448 (scale_fmt None)                 */
+#define FLYAI_LIN_FMT_UE8M0   1  /* activation scale 2^ceil(log2(amax/448)) (scale_fmt "ue8m0") */
+
+/* Bytes of the packed weight bank of an [N, K] weight. */
+FLYAI_API int flyai_fp8_linear_bank_bytes(int32_t N, int32_t K, size_t* bytes);
+/* Pack weight (e4m3 [N, K], 16-byte aligned) and its scales (scale_dtype
+ * FLYAI_LIN_SCALE_*) into bank, at load time (the reference's Linear holds
+ * weight + weight.scale, model.py:127-158).  Banks of weights that read the same
+ * x concatenate: the bank of [w1; w3] is the bank of w1 followed by that of w3. */
+FLYAI_API int flyai_fp8_linear_pack(int32_t N, int32_t K, const void* weight, const void* scale,
+                                    int32_t scale_dtype, void* bank, void* stream);
+/* Workspace bytes for calls of up to max_tokens rows.  Zero-fill it once before
+ * its first use; int32 word 0 is the error word (bit 1: a bounded wait gave up),
+ * which calls set and never clear. */
+FLYAI_API int flyai_fp8_linear_workspace_bytes(int32_t max_tokens, int32_t N, int32_t K,
+                                               size_t* bytes);
+/* y = linear(x, W) for num_tokens rows (two kernel launches per 64 rows),
+ * scale_fmt FLYAI_LIN_FMT_*; x 16-byte and workspace 256-byte aligned. */
+FLYAI_API int flyai_fp8_linear(int32_t num_tokens, int32_t N, int32_t K, const void* x,
+                               const void* bank, int32_t scale_fmt, void* y, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
