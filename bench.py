@@ -9,14 +9,15 @@ roofline of the expert-streaming kernels, and the reference CPU path timed on
 this host.  At N=1 the line also carries "families": the DeepSeek-V3 FP8 layer
 (config 3), the MiniMax-M2.5 NVFP4 layer (config 4, with its M=4096 prefill) and
 the DeepSeek-V4-Flash W4A8 layer, each with its verify-size sweep, expert-kernel
-roofline, end-to-end time and CPU oracle timing.
+roofline, end-to-end time and CPU oracle timing, and "linear": the seven dense
+FP8 GEMMs of a DeepSeek-V4-Flash decode layer (flyai_fp8_linear).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
 N>1 (torchrun, one rank per GPU): expert parallel -- rank r holds experts
-[r*E/N, (r+1)*E/N); per step x is broadcast from rank 0, every rank routes the
-same tokens, computes its experts' weighted pair rows, an NCCL all-reduce
-rebuilds all rows (other shards contribute zeros) and each rank folds them.
+[r*E/N, (r+1)*E/N); every rank holds the step's tokens, routes them, computes
+its experts' weighted rows in one launch and publishes them to its peers over
+NVLink peer memory; each rank folds all shards' rows in ascending expert id.
 Total work is fixed, so scaling is strong; time is the max over ranks.
 """
 import argparse
@@ -38,6 +39,27 @@ from flyai_b200 import synth  # noqa: E402
 METRIC = "MoE layer us at M=5 verify (GPT-OSS-120B MXFP4, E=128 top-4, H=I=2880)"
 H = I = 2880
 E, K_TOP = 128, 4
+
+
+class L2Flush:
+    """Evicts the L2 (126 MB) before every timed step.  "write" (default): a
+    256 MiB write; "writeread": that write, then a 256 MiB read, so the write's
+    dirty lines are written back to HBM before the step instead of during it (on
+    the GPT-OSS verify layer the two measure the same, within 0.5 %)."""
+
+    def __init__(self, dev, mode="write"):
+        self.mode = mode
+        self.w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        self.r = torch.ones(32 << 20, dtype=torch.int64, device=dev) if mode == "writeread" else None
+        self.sink = torch.empty((), dtype=torch.int64, device=dev)
+        self.note = ("flushed before every timed step: 256 MiB written, then 256 MiB read "
+                     "(the written lines' write-backs finish before the step)" if mode == "writeread"
+                     else "flushed (256 MiB write) before every timed step")
+
+    def __call__(self):
+        self.w.zero_()
+        if self.r is not None:
+            torch.sum(self.r, dim=0, out=self.sink)
 
 
 def parse():
@@ -64,6 +86,11 @@ def parse():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--sustain", type=int, default=2000,
                    help="untimed steps run under the clock sampler before timing")
+    p.add_argument("--l2", default="write", choices=["write", "writeread"],
+                   help="L2 flush before each timed step: a 256 MiB write (default), or the "
+                        "write then a 256 MiB read (its write-backs finish before the step)")
+    p.add_argument("--no-linear", action="store_true",
+                   help="default run: leave out the dense FP8 linear sub-object")
     return p.parse_args()
 
 
@@ -272,7 +299,7 @@ def main():
     moe = Mxfp4MoE.from_layer(layer, expert_range=(lo, hi), max_tokens=max_tok, device=dev)
     x = synth.make_tokens(M, H, seed=args.seed, device=dev)
     y = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev, args.l2)
 
 
     ep = None
@@ -291,10 +318,10 @@ def main():
         ctx = sampler if sampler is not None else _Null()
         ctx.__enter__()
         for _ in range(warmup):
-            flush.zero_()
+            flush()
             step()
         for _ in range(sustain_iters):          # clocks settle under load (same count on every rank)
-            flush.zero_()
+            flush()
             step()
         torch.cuda.synchronize()
         if dist:
@@ -304,7 +331,7 @@ def main():
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
         n0 = launch_count()
         for i in range(steps):
-            flush.zero_()
+            flush()
             starts[i].record()
             step()
             ends[i].record()
@@ -359,11 +386,11 @@ def main():
     k0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     k1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     for _ in range(args.warmup):
-        flush.zero_()
+        flush()
         layer_step(x, y)
     torch.cuda.synchronize()
     for i in range(args.steps):
-        flush.zero_()
+        flush()
         set_profile_events(k0[i], k1[i])
         layer_step(x, y)
     set_profile_events(None, None)
@@ -386,7 +413,7 @@ def main():
         "data": "synthetic (seeded; BASELINE config 1 distributions)",
         "config": {"workload": "gpt-oss-120b MoE layer verify M=5 (config 1)", "experts": E,
                    "top_k": K_TOP, "hidden": H, "inter": I, "tokens": M,
-                   "parallelism": f"ep{world}", "l2": "flushed (256 MiB write) before every timed step",
+                   "parallelism": f"ep{world}", "l2": flush.note,
                    **({"ep_tokens": "replicated on every rank"} if world > 1 else {})},
         "e2e": {"value": round(e2e_ms * 1e3, 2), "unit": "us", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
@@ -441,6 +468,8 @@ def main():
                                     tokens=FAMILY_TOKENS[wl], compact=True)
             torch.cuda.empty_cache()
         result["families"] = fam
+    if world == 1 and not args.no_linear:
+        result["linear"] = linear_result(args, dev, flush)
     if rank == 0:
         print(json.dumps(result), flush=True)
     if ep is not None:
@@ -534,7 +563,7 @@ def family_result(args, workload, world, rank, dev, dist, steps, warmup, sustain
 
         def kernel_bytes_of(distinct):
             return distinct * od.expert_bytes(Hd, Id) + od.shared_bytes(Hd, Id)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev, args.l2)
     Hd, Id, Ed, Kd = layer.hidden, layer.inter, layer.num_experts, layer.top_k
     hbm_peak, peak_kind = peaks()
     ep = None
@@ -562,7 +591,7 @@ def family_result(args, workload, world, rank, dev, dist, steps, warmup, sustain
         x = synth.make_tokens(M, Hd, seed=args.seed + M, device=dev)
         y = torch.empty_like(x)
         for _ in range(warmup + sustain):
-            flush.zero_()
+            flush()
             layer_step(x, y)
         torch.cuda.synchronize()
         if dist:
@@ -574,7 +603,7 @@ def family_result(args, workload, world, rank, dev, dist, steps, warmup, sustain
         kv = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         n0 = launch_count()
         for i in range(steps):
-            flush.zero_()
+            flush()
             ev[i][0].record()
             layer_step(x, y)
             ev[i][1].record()
@@ -582,7 +611,7 @@ def family_result(args, workload, world, rank, dev, dist, steps, warmup, sustain
         ctx.__exit__(None, None, None)
         launches = launch_count() - n0
         for i in range(steps):          # the expert kernel alone, same calls
-            flush.zero_()
+            flush()
             set_profile_events(*kv[i])
             layer_step(x, y)
         set_profile_events(None, None)
@@ -630,7 +659,7 @@ def family_result(args, workload, world, rank, dev, dist, steps, warmup, sustain
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     for i in range(steps):
-        flush.zero_()
+        flush()
         ev[i][0].record()
         x_in.copy_(x_h, non_blocking=True)
         layer_step(x_in, y)
@@ -647,7 +676,7 @@ def family_result(args, workload, world, rank, dev, dist, steps, warmup, sustain
         "data": f"synthetic (seeded; {data_cfg})",
         "config": {"workload": wl_name, "experts": Ed, "top_k": Kd, "hidden": Hd, "inter": Id,
                    "tokens": M, "parallelism": f"ep{world}",
-                   "l2": "flushed (256 MiB write) before every timed step", **cfg_extra},
+                   "l2": flush.note, **cfg_extra},
         "e2e": {"value": round(e2e_ms * 1e3, 2), "unit": "us", "h2d_bytes_per_step": M * Hd * 2,
                 "d2h_bytes_per_step": M * Hd * 2},
         "gpu_launches": head["launches"],
@@ -726,6 +755,92 @@ def family_result(args, workload, world, rank, dev, dist, steps, warmup, sustain
     return result
 
 
+def linear_result(args, dev, flush):
+    """The seven dense FP8 GEMMs of a DeepSeek-V4-Flash decode layer
+    (engines/deepseek_v4/v4_fp8_gemv.py:6-14): attention wq_a, wkv, wq_b, wo_b, the
+    indexer's wq_b, the shared expert's w1 and w3 as one stacked bank, and its w2;
+    e4m3 weights with e8m0 128x128 block scales, ue8m0 activation scales.  Per token
+    count: microseconds for the seven in sequence (L2 flushed before each layer),
+    each GEMM alone, and the weight stream's roofline (weight bytes / time)."""
+    from flyai_b200.linear import Fp8Linear
+    from flyai_b200.moe import launch_count
+    from oracle.fp8_linear import weight_bytes
+    L = synth.V4_LINEARS
+    specs = [("wq_a", ["wq_a"]), ("wkv", ["wkv"]), ("wq_b", ["wq_b"]), ("wo_b", ["wo_b"]),
+             ("idx_wq_b", ["idx_wq_b"]), ("shared_w13", ["shared_w1", "shared_w3"]),
+             ("shared_w2", ["shared_w2"])]
+    lins = []
+    for i, (name, parts) in enumerate(specs):
+        made = [synth.make_fp8_linear(*L[pn], seed=args.seed + 7 * i + j, device=dev)
+                for j, pn in enumerate(parts)]
+        lin = Fp8Linear([w for w, _ in made], [s for _, s in made], scale_fmt="ue8m0", max_tokens=8,
+                        device=dev)
+        lins.append((name, lin, sum(weight_bytes(*L[pn], e8m0=True) for pn in parts)))
+        del made
+    total_bytes = sum(b for _, _, b in lins)
+    hbm_peak, peak_kind = peaks()
+
+    def graphed(fn):
+        """fn captured in a CUDA graph (a decode step replays its layers that way),
+        so the timed region holds no host launch gaps."""
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        return g
+
+    def time_steps(g, steps, warmup):
+        for _ in range(warmup):
+            flush()
+            g.replay()
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        for a, b in ev:
+            flush()
+            a.record()
+            g.replay()
+            b.record()
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in ev) / steps
+
+    out = {}
+    for M in (1, 4):
+        xs = [synth.make_tokens(M, lin.K, seed=args.seed + 100 + i, device=dev)
+              for i, (_, lin, _) in enumerate(lins)]
+        ys = [torch.empty(M, lin.N, dtype=torch.bfloat16, device=dev) for _, lin, _ in lins]
+
+        def layer():
+            for (_, lin, _), x, y in zip(lins, xs, ys):
+                lin(x, out=y)
+        n0 = launch_count()
+        layer()
+        launches = launch_count() - n0
+        ms = time_steps(graphed(layer), args.steps, args.warmup)
+        each = {}
+        for (name, lin, nbytes), x, y in zip(lins, xs, ys):
+            ems = time_steps(graphed(lambda: lin(x, out=y)), args.steps, args.warmup)
+            each[name] = {"us": round(ems * 1e3, 2), "gbs": round(nbytes / (ems * 1e-3) / 1e9, 1)}
+        for _, lin, _ in lins:
+            assert lin.read_error() == 0
+        gbs = total_bytes / (ms * 1e-3) / 1e9
+        out[f"M{M}"] = {"us_per_layer": round(ms * 1e3, 2), "gpu_launches_per_layer": launches,
+                        "timing": "CUDA graph of the seven calls, replayed; CUDA events",
+                        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak,
+                                     "unit": "GB/s", "frac": round(gbs / hbm_peak, 4),
+                                     "peak_source": peak_kind,
+                                     "kernel": "ln_gemm_kernel (+ ln_quant_kernel, ln_reduce_kernel)"},
+                        "each": each}
+    return {"workload": "DeepSeek-V4-Flash decode layer: 7 dense FP8 GEMMs (fp8 e4m3 + e8m0 128x128)",
+            "weight_bytes_per_layer": total_bytes, "l2": flush.note,
+            "data": "synthetic (seeded N(0,1) e4m3 weights, e8m0 scales 2^-10..2^-7, bf16 N(0,1) x)",
+            **out}
+
+
 def m25_prefill(args, layer, erange, world, dev, flush, max_over_ranks, hbm_peak):
     """Config 4's prefill batch (M=4096 by default) through the same layer: the
     NVFP4 prefill path (weights expanded to bf16 in shared memory, tcgen05
@@ -752,19 +867,19 @@ def m25_prefill(args, layer, erange, world, dev, flush, max_over_ranks, hbm_peak
 
     steps = max(3, min(args.steps, 10))
     for _ in range(3):
-        flush.zero_()
+        flush()
         step()
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     kv = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     for i in range(steps):
-        flush.zero_()
+        flush()
         ev[i][0].record()
         step()
         ev[i][1].record()
     torch.cuda.synchronize()
     for i in range(steps):
-        flush.zero_()
+        flush()
         set_profile_events(*kv[i])
         step()
     set_profile_events(None, None)

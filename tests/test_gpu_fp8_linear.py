@@ -75,6 +75,20 @@ def test_wide_bank_matches_oracle_on_sampled_rows():
     assert_linear_close(y[:, rows], ref)
 
 
+def test_long_k_matches_oracle_on_sampled_rows():
+    """K = 32768 (256 K blocks, 64 pieces per row block) at 16 tokens."""
+    N, K = 4096, 32768
+    w, s = synth.make_fp8_linear(N, K, seed=13, e8m0=False, device="cuda")
+    lin = Fp8Linear(w, s, scale_fmt=None, max_tokens=16)
+    x = synth.make_tokens(16, K, seed=13)
+    y = lin(x.cuda()).float().cpu().numpy()
+    rows = np.r_[0:128, 2048:2176, N - 128:N]
+    wr = w.view(torch.uint8)[torch.as_tensor(rows, device="cuda")].cpu().numpy()
+    sr = s.cpu().numpy()[rows[::128] // 128]
+    assert_linear_close(y[:, rows], ol.linear(x.float().numpy(), wr, sr, None))
+    assert lin.read_error() == 0
+
+
 def test_stacked_bank_is_the_concatenation():
     """[w1; w3] as one bank = the two linears side by side, bit for bit: the
     arithmetic of an output depends on K only, not on which CTA computed it."""
