@@ -30,7 +30,8 @@ static int check_desc(const flyai_moe_desc* d) {
   for (int i = 0; i < 4; ++i)
     if (d->reserved[i] != 0) return FLYAI_ERR_INVALID_ARG;
   if (d->num_experts < 1 || d->num_experts > 1024) return FLYAI_ERR_INVALID_ARG;
-  if (d->top_k < 1 || d->top_k > kMaxTopK || d->top_k > d->num_experts)
+  const int max_k = d->gating == FLYAI_GATE_EXTERNAL ? kMaxTopKExternal : kMaxTopK;
+  if (d->top_k < 1 || d->top_k > max_k || d->top_k > d->num_experts)
     return FLYAI_ERR_INVALID_ARG;
   if (d->hidden < 32 || d->inter < 32) return FLYAI_ERR_INVALID_ARG;
   if (d->hidden % 32 || d->inter % 32) return FLYAI_ERR_ALIGNMENT;
@@ -38,13 +39,21 @@ static int check_desc(const flyai_moe_desc* d) {
     return FLYAI_ERR_INVALID_ARG;
   if (d->max_tokens < 0) return FLYAI_ERR_INVALID_ARG;
   if (d->format == FLYAI_FMT_MXFP4) {
-    if (d->gating != FLYAI_GATE_SOFTMAX_TOPK) return FLYAI_ERR_UNSUPPORTED;
-    if (d->activation != FLYAI_ACT_GPTOSS_SWIGLU) return FLYAI_ERR_UNSUPPORTED;
+    // GPT-OSS (routed here, SwiGLU) or Kimi-K3 (routed by the caller, situ)
+    const bool k3 = d->gating == FLYAI_GATE_EXTERNAL;
+    if (!k3 && d->gating != FLYAI_GATE_SOFTMAX_TOPK) return FLYAI_ERR_UNSUPPORTED;
+    if (d->activation != (k3 ? FLYAI_ACT_SITU : FLYAI_ACT_GPTOSS_SWIGLU)) return FLYAI_ERR_UNSUPPORTED;
     // the tcgen05 kernels: K-tiles of 64, one tensor-memory accumulator row block
     if (d->hidden % 64 || d->inter % 64) return FLYAI_ERR_ALIGNMENT;
     if (d->hidden > kTcMaxK || d->inter > kTcMaxK) return FLYAI_ERR_UNSUPPORTED;
     if (d->n_group != 0 || d->topk_group != 0 || d->route_scale != 0.f || d->n_shared != 0)
       return FLYAI_ERR_INVALID_ARG;
+    if (k3) {
+      // beta > 0, linear_beta >= 0 (0 = None); the verify-size kernels only
+      if (!(d->swiglu_alpha > 0.f) || !(d->swiglu_limit >= 0.f)) return FLYAI_ERR_INVALID_ARG;
+      if (d->max_tokens >= kTcPrefillMinTokens) return FLYAI_ERR_UNSUPPORTED;
+      return FLYAI_OK;
+    }
     if (!(d->swiglu_limit > 0.f) || !(d->swiglu_alpha > 0.f)) return FLYAI_ERR_INVALID_ARG;
     return FLYAI_OK;
   }
@@ -292,6 +301,7 @@ int flyai_moe_route(const flyai_moe_desc* desc, int32_t M, const void* x,
                     const flyai_moe_weights* w, void* logits, int32_t* topk_ids,
                     void* topk_weights, void* workspace, size_t workspace_bytes, void* stream) {
   FLYAI_TRY(check_desc(desc));
+  if (desc->gating == FLYAI_GATE_EXTERNAL) return FLYAI_ERR_UNSUPPORTED;   // flyai_moe_route_ids
   FLYAI_TRY(check_tokens(desc, M));
   FLYAI_TRY(check_workspace(desc, workspace, workspace_bytes));
   FLYAI_TRY(check_weights(desc, w, true, false));
@@ -342,6 +352,20 @@ int flyai_moe_route_logits(const flyai_moe_desc* desc, int32_t M, const void* x,
   const Fp8Workspace fw = carve_fp8_workspace(*desc, desc->max_tokens, workspace);
   return launch_layer_route(*desc, M, x, *w, nullptr, topk_ids, static_cast<float*>(topk_weights), fw,
                             static_cast<cudaStream_t>(stream), router_logits);
+}
+
+int flyai_moe_route_ids(const flyai_moe_desc* desc, int32_t M, const int32_t* topk_ids,
+                        const float* topk_weights, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  FLYAI_TRY(check_desc(desc));
+  if (desc->gating != FLYAI_GATE_EXTERNAL) return FLYAI_ERR_UNSUPPORTED;
+  FLYAI_TRY(check_tokens(desc, M));
+  FLYAI_TRY(check_workspace(desc, workspace, workspace_bytes));
+  if (M > 0 && (!topk_ids || !topk_weights)) return FLYAI_ERR_INVALID_ARG;
+  if ((topk_ids && !aligned(topk_ids, 4)) || (topk_weights && !aligned(topk_weights, 4)))
+    return FLYAI_ERR_ALIGNMENT;
+  const Workspace ws = carve_workspace(*desc, desc->max_tokens, workspace);
+  return launch_route_ids(*desc, M, topk_ids, topk_weights, ws, static_cast<cudaStream_t>(stream));
 }
 
 int flyai_moe_read_plan(const flyai_moe_desc* desc, int32_t M, const void* workspace,
@@ -466,6 +490,8 @@ int flyai_moe_forward(const flyai_moe_desc* desc, int32_t M, const void* x,
                       void* topk_weights, void* workspace, size_t workspace_bytes,
                       void* stream) {
   FLYAI_TRY(check_desc(desc));
+  // caller-routed layers: flyai_moe_route_ids + flyai_moe_experts
+  if (desc->gating == FLYAI_GATE_EXTERNAL) return FLYAI_ERR_UNSUPPORTED;
   FLYAI_TRY(check_tokens(desc, M));
   FLYAI_TRY(check_workspace(desc, workspace, workspace_bytes));
   FLYAI_TRY(check_weights(desc, w, true, true));
@@ -551,8 +577,9 @@ static int check_ep(const flyai_moe_desc* desc, int32_t M, const flyai_moe_ep_pe
     return FLYAI_ERR_INVALID_ARG;
   for (int r = 0; r < ep->world; ++r)
     if (!ep->mailbox[r] || !aligned(ep->mailbox[r], 256)) return FLYAI_ERR_INVALID_ARG;
-  // peer-memory exchange exists for the MXFP4 tcgen05 verify kernel only
-  if (is_fp8(*desc) || M >= kTcPrefillMinTokens) return FLYAI_ERR_UNSUPPORTED;
+  // peer-memory exchange exists for the GPT-OSS MXFP4 tcgen05 verify kernel only
+  if (is_fp8(*desc) || M >= kTcPrefillMinTokens || desc->gating == FLYAI_GATE_EXTERNAL)
+    return FLYAI_ERR_UNSUPPORTED;
   return FLYAI_OK;
 }
 

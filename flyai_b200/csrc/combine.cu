@@ -1,4 +1,4 @@
-// Weighted combine of the MXFP4 (GPT-OSS) layer: y[t] = bf16 fold of the
+// Weighted combine of the MXFP4 layers.  GPT-OSS: y[t] = bf16 fold of the
 // token's k weighted expert rows in ascending expert id with a bf16 rounding
 // after every add -- the order and rounding of the reference's index_add_ loop
 // (transformers/models/gpt_oss/modeling_gpt_oss.py:96-112).  One CTA per
@@ -49,6 +49,49 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
   int order[kMaxTopK];
   slots_by_expert(ids, blockIdx.x, k, order);
   fold_rows(pair_out, order, blockIdx.x, k, H, true, y);
+}
+
+// Kimi-K3 (FLYAI_ACT_SITU): y[t] = bf16 of the fp32 sum over the k slots, in slot
+// order, of (bf16 w2 row) x (fp32 routing weight) -- moe_infer's
+// new_x.view(T, k, H).type(fp32).mul_(w).sum(dim=1).type(bf16)
+// (vendor/kimi_k3_ref/modeling_kimi_linear.py:868-874).  The pair rows are unweighted.
+__global__ void __launch_bounds__(256) combine_slots_kernel(const uint16_t* __restrict__ pair_out,
+                                                            const float* __restrict__ wts, int k,
+                                                            int H, uint16_t* __restrict__ y) {
+  pdl_wait();
+  const int m = blockIdx.x;
+  float w[kMaxTopKExternal];
+#pragma unroll
+  for (int s = 0; s < kMaxTopKExternal; ++s) w[s] = s < k ? __ldg(&wts[m * k + s]) : 0.f;
+  for (int o = (blockIdx.y * blockDim.x + threadIdx.x) * 8; o < H; o += gridDim.y * blockDim.x * 8) {
+    uint4 v[kMaxTopKExternal];
+#pragma unroll
+    for (int s = 0; s < kMaxTopKExternal; ++s)
+      if (s < k)
+        v[s] = __ldcg(reinterpret_cast<const uint4*>(pair_out + (static_cast<size_t>(m) * k + s) * H + o));
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+    for (int s = 0; s < kMaxTopKExternal; ++s) {
+      if (s < k) {
+        const uint32_t u[4] = {v[s].x, v[s].y, v[s].z, v[s].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float lo = __fmul_rn(__uint_as_float(u[j] << 16), w[s]);
+          const float hi = __fmul_rn(__uint_as_float(u[j] & 0xFFFF0000u), w[s]);
+          acc[2 * j] = s == 0 ? lo : __fadd_rn(acc[2 * j], lo);
+          acc[2 * j + 1] = s == 0 ? hi : __fadd_rn(acc[2 * j + 1], hi);
+        }
+      }
+    }
+    uint4 out;
+    out.x = float_to_bf16_bits(acc[0]) | (static_cast<uint32_t>(float_to_bf16_bits(acc[1])) << 16);
+    out.y = float_to_bf16_bits(acc[2]) | (static_cast<uint32_t>(float_to_bf16_bits(acc[3])) << 16);
+    out.z = float_to_bf16_bits(acc[4]) | (static_cast<uint32_t>(float_to_bf16_bits(acc[5])) << 16);
+    out.w = float_to_bf16_bits(acc[6]) | (static_cast<uint32_t>(float_to_bf16_bits(acc[7])) << 16);
+    *reinterpret_cast<uint4*>(y + static_cast<size_t>(m) * H + o) = out;
+  }
 }
 
 // Expert-parallel combine: wait (bounded, ~2 s) until every rank raised its flag
@@ -131,10 +174,15 @@ int launch_combine(const flyai_moe_desc& d, int M, const uint16_t* pair_out, voi
                    const Workspace& ws, cudaStream_t stream) {
   if (M == 0) return FLYAI_OK;
   const int32_t* ids = ws.ids;
+  const float* wts = ws.wts;
   int k = d.top_k, H = d.hidden;
   uint16_t* yo = static_cast<uint16_t*>(y);
   void* args[] = {&pair_out, &ids, &k, &H, &yo};
-  const cudaError_t st = launch_fold(d, M, stream, reinterpret_cast<void (*)()>(combine_kernel), args);
+  void* args_slots[] = {&pair_out, &wts, &k, &H, &yo};
+  const cudaError_t st =
+      d.activation == FLYAI_ACT_SITU
+          ? launch_fold(d, M, stream, reinterpret_cast<void (*)()>(combine_slots_kernel), args_slots)
+          : launch_fold(d, M, stream, reinterpret_cast<void (*)()>(combine_kernel), args);
   note_launch();
   return st == cudaSuccess ? FLYAI_OK : FLYAI_ERR_CUDA;
 }

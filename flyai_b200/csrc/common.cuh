@@ -14,6 +14,7 @@ namespace flyai {
 void note_launch(int n = 1);
 
 constexpr int kMaxTopK = 8;
+constexpr int kMaxTopKExternal = 16;   // FLYAI_GATE_EXTERNAL (Kimi-K3) layers
 
 // ---- bf16 arithmetic with the reference's rounding points -------------------
 // The reference materialises every elementwise result in bf16 (torch CPU ops on
@@ -210,6 +211,7 @@ __device__ __forceinline__ uint32_t lds32(const void* p) {
 
 // Error bits a kernel can leave in the workspace (read back with flyai_moe_read_error).
 constexpr int32_t kErrWaitTimeout = 1;
+constexpr int32_t kErrBadIndex = 2;   // an expert id or table entry out of range (read as 0)
 
 // Expert-parallel mailbox (flyai_moe_ep_alloc): kEpFlagBytes of flag words, then
 // the pair-row buffers.  Word r = the last epoch rank r finished; word

@@ -170,7 +170,6 @@ struct F8RouteParams {
   int32_t* err;          // error word (bit 2: an input id or table entry out of range)
 };
 
-constexpr int32_t kErrBadIndex = 2;
 
 // The gate's score of a logit: sigmoid (DeepSeek-V3, MiniMax-M2) or
 // sqrt(softplus) with torch's threshold 20 (DeepSeek-V4, model.py:575-576).

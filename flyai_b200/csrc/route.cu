@@ -477,4 +477,47 @@ int launch_route(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_
   return cudaGetLastError() == cudaSuccess ? FLYAI_OK : FLYAI_ERR_CUDA;
 }
 
+// ---------------------------------------------------------------------------
+// Routing chosen by the caller (Kimi-K3's moe_infer seam): the ids are checked
+// against [0, E) -- the expert kernels index the bank with them -- and copied
+// with the weights; then the plan as for routed batches.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) route_ids_kernel(const int32_t* __restrict__ ids_in,
+                                                        const float* __restrict__ wts_in, int P, int E,
+                                                        int32_t* __restrict__ ids, float* __restrict__ wts,
+                                                        int32_t* err) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < P; i += gridDim.x * blockDim.x) {
+    int e = __ldg(&ids_in[i]);
+    if (e < 0 || e >= E) {
+      atomicOr(err, kErrBadIndex);
+      e = 0;
+    }
+    ids[i] = e;
+    wts[i] = __ldg(&wts_in[i]);
+  }
+}
+
+int launch_route_ids(const flyai_moe_desc& d, int M, const int32_t* ids, const float* wts,
+                     const Workspace& ws, cudaStream_t stream) {
+  const int k = d.top_k, P = M * k, El = d.expert_end - d.expert_begin;
+  if (P == 0) return FLYAI_OK;
+  route_ids_kernel<<<(P + 255) / 256, 256, 0, stream>>>(ids, wts, P, d.num_experts, ws.ids, ws.wts,
+                                                         ws.err);
+  note_launch();
+  const size_t psmem = plan_smem_bytes(P, El, 32);
+  if (psmem > 48 * 1024 &&
+      cudaFuncSetAttribute(route_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(psmem)) != cudaSuccess)
+    return FLYAI_ERR_CUDA;
+  route_plan_kernel<<<1, 1024, psmem, stream>>>(ws.ids, P, d.expert_begin, El, ws.counts, ws.offsets,
+                                                ws.active, ws.n_active, ws.perm, ws.n_chunks,
+                                                ws.chunk_slot, ws.chunk_c0, ws.max_chunks, ws.fold_ticket,
+                                                M * (d.hidden / 16), k, ws.chunk_info, ws.chunk_rows,
+                                                ws.chunk_done);
+  note_launch();
+  return cudaGetLastError() == cudaSuccess ? FLYAI_OK : FLYAI_ERR_CUDA;
+}
+
 }  // namespace flyai

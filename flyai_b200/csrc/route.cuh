@@ -6,6 +6,10 @@ namespace flyai {
 int launch_route(const flyai_moe_desc& d, int M, const void* x, const flyai_moe_weights& w,
                  void* logits_out, int32_t* ids_out, void* wts_out, const Workspace& ws,
                  cudaStream_t stream);
+// Routing the caller chose (FLYAI_GATE_EXTERNAL): ids and weights into the
+// workspace, an id outside [0, E) read as 0 with kErrBadIndex, then the plan.
+int launch_route_ids(const flyai_moe_desc& d, int M, const int32_t* ids, const float* wts,
+                     const Workspace& ws, cudaStream_t stream);
 
 // Tensor-core (tcgen05 kind::mxf4) expert path: every MXFP4 descriptor the ABI
 // accepts (hidden and inter multiples of 64, at most kTcMaxK); the bank layout is

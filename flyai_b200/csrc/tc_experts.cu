@@ -34,9 +34,16 @@ size_t tc_packed_bytes(const flyai_moe_desc& d, int proj) {
   return tc_layout(d, proj).expert_bytes * static_cast<size_t>(d.expert_end - d.expert_begin);
 }
 
+// Bank row -> source row.  The W13 bank interleaves gate and up rows (gate j at
+// 2j, up j at 2j+1: GPT-OSS's gate_up_proj order); a source holding w1's rows then
+// w3's (split = inter) is interleaved on the way.
+__device__ __forceinline__ int tc_src_row(int row, int split) {
+  return split ? ((row & 1) ? split + (row >> 1) : (row >> 1)) : row;
+}
+
 // One thread per 16-byte chunk (one 32-element scale group of one row).
 __global__ void tc_pack_data_kernel(const uint8_t* __restrict__ blocks,
-                                    uint8_t* __restrict__ packed, int E, TcLayout L) {
+                                    uint8_t* __restrict__ packed, int E, TcLayout L, int split) {
   const size_t per_expert = static_cast<size_t>(L.R) * L.G;
   const size_t total = per_expert * E;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
@@ -49,13 +56,13 @@ __global__ void tc_pack_data_kernel(const uint8_t* __restrict__ blocks,
     uint8_t* dst = packed + static_cast<size_t>(e) * L.expert_bytes + tc_tile_offset(L, mt, kt) +
                    static_cast<size_t>(c) * rows_t * 16 + (r >> 3) * 128 + (r & 7) * 16;
     *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(
-        blocks + ((static_cast<size_t>(e) * L.R + row) * L.G + g) * 16);
+        blocks + ((static_cast<size_t>(e) * L.R + tc_src_row(row, split)) * L.G + g) * 16);
   }
 }
 
 // One thread per scale slot of every tile's chunks (rows padded to 128).
 __global__ void tc_pack_scale_kernel(const uint8_t* __restrict__ scales,
-                                     uint8_t* __restrict__ packed, int E, TcLayout L) {
+                                     uint8_t* __restrict__ packed, int E, TcLayout L, int split) {
   const int chunks_full = kKT / 128;
   const size_t per_mtile = static_cast<size_t>(L.NKT) * chunks_full * 512;
   const size_t total = per_mtile * L.MT * E;
@@ -74,7 +81,8 @@ __global__ void tc_pack_scale_kernel(const uint8_t* __restrict__ scales,
     const int g = kt * (kKT / 32) + (off / 512) * 4 + b % 4;
     const int rows_t = tc_rows(L, mt);
     uint8_t v = 127;                                      // neutral scale for padding
-    if (r < rows_t && g < L.G) v = scales[(static_cast<size_t>(e) * L.R + mt * 128 + r) * L.G + g];
+    if (r < rows_t && g < L.G)
+      v = scales[(static_cast<size_t>(e) * L.R + tc_src_row(mt * 128 + r, split)) * L.G + g];
     packed[static_cast<size_t>(e) * L.expert_bytes + tc_tile_offset(L, mt, kt) +
            static_cast<size_t>(rows_t) * (kt_len / 2) + off] = v;
   }
@@ -85,11 +93,13 @@ int launch_tc_pack(const flyai_moe_desc& d, int proj, const void* blocks, const 
   const TcLayout L = tc_layout(d, proj);
   const int El = d.expert_end - d.expert_begin;
   if (El == 0) return FLYAI_OK;
+  // FLYAI_ACT_SITU W13 sources are [w1; w3]
+  const int split = (d.activation == FLYAI_ACT_SITU && proj == FLYAI_PROJ_W13) ? d.inter : 0;
   tc_pack_data_kernel<<<2368, 256, 0, stream>>>(static_cast<const uint8_t*>(blocks),
-                                                static_cast<uint8_t*>(packed), El, L);
+                                                static_cast<uint8_t*>(packed), El, L, split);
   note_launch();
   tc_pack_scale_kernel<<<1184, 256, 0, stream>>>(static_cast<const uint8_t*>(scales),
-                                                 static_cast<uint8_t*>(packed), El, L);
+                                                 static_cast<uint8_t*>(packed), El, L, split);
   note_launch();
   return cudaGetLastError() == cudaSuccess ? FLYAI_OK : FLYAI_ERR_CUDA;
 }
@@ -135,7 +145,8 @@ struct TcParams {
   uint8_t* h_sf;
   uint16_t* pair_out;         // [P, H] weighted expert rows, flat pair order
   int hidden, inter, kmax;
-  float limit, alpha;
+  float limit, alpha;         // GPT-OSS clamp and alpha; situ: linear_beta (0 = none) and beta
+  int situ;                   // FLYAI_ACT_SITU: Kimi-K3 activation, unweighted pair rows
   int32_t* err;
   // expert parallel over peer memory (ep_world > 0): pair rows go to every
   // rank's mailbox instead of pair_out, then this rank's flag is raised in each
@@ -234,8 +245,18 @@ __host__ __device__ inline TcSmem tc_smem_layout(int kmax, size_t tile_full, boo
 }
 
 
-// Down epilogue: weighted pair rows (flat pair order); the combine kernel
-// folds each token's k rows afterwards.
+// Kimi-K3 `situ` of one (gate, up) pair of bf16 Linear outputs, in fp32 as
+// SituAndMul.forward computes it (vendor/kimi_k3_ref/modeling_kimi_linear.py:75-80):
+// beta*tanh(g/beta) * sigmoid(g) * (lb*tanh(u/lb), or u when lb is 0), to bf16.
+__device__ __forceinline__ float tc_situ(float g, float u, float beta, float lb) {
+  const float sg = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-g)));
+  const float a = __fmul_rn(__fmul_rn(beta, tanhf(__fdiv_rn(g, beta))), sg);
+  const float uu = lb > 0.f ? __fmul_rn(lb, tanhf(__fdiv_rn(u, lb))) : u;
+  return bf16r(__fmul_rn(a, uu));
+}
+
+// Down epilogue: weighted pair rows (flat pair order; situ layers: the bf16 w2
+// outputs unweighted); the combine kernel folds each token's k rows afterwards.
 __device__ __forceinline__ void tc_epilogue_down(const TcParams& p, const float (&val)[kTcChunk],
                                                  int nt, int pos0, int mt, int q, int lane,
                                                  float bias_v, const int32_t* perm,
@@ -246,7 +267,7 @@ __device__ __forceinline__ void tc_epilogue_down(const TcParams& p, const float 
     const int flat = perm[pos0 + i];
     float v = bf16r(val[i]);
     if (p.dn.bias) v = bf16r(__fadd_rn(v, bias_v));
-    v = bf16r(__fmul_rn(v, wts[flat]));
+    if (!p.situ) v = bf16r(__fmul_rn(v, wts[flat]));   // situ rows: the combine weighs them
     const uint16_t b = float_to_bf16_bits(v);
     const size_t at = static_cast<size_t>(flat) * p.hidden + o;
     if (p.ep_world == 0) {
@@ -762,7 +783,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_moe_kernel(const __grid_cons
           const float upv = __shfl_xor_sync(0xffffffffu, val[i], 1);
           if (even) {
             float h = 0.f;
-            if (i < nt && row < P.L.R) {
+            if (i < nt && row < P.L.R && p.situ) {
+              h = tc_situ(bf16r(val[i]), bf16r(upv), p.alpha, p.limit);
+            } else if (i < nt && row < P.L.R) {
               float gate = bf16r(val[i]);
               float up = bf16r(upv);
               if (P.bias) {
@@ -1001,6 +1024,7 @@ int launch_tc_experts(const flyai_moe_desc& d, int M, const void* x, bool x_spli
   prm.kmax = d.hidden > d.inter ? d.hidden : d.inter;
   prm.limit = d.swiglu_limit;
   prm.alpha = d.swiglu_alpha;
+  prm.situ = d.activation == FLYAI_ACT_SITU;
   prm.err = ws.err;
   if (ep) {
     const size_t rows_bytes = static_cast<size_t>(d.max_tokens) * d.top_k * d.hidden * 2;
@@ -1027,7 +1051,7 @@ int launch_tc_experts(const flyai_moe_desc& d, int M, const void* x, bool x_spli
 }
 
 bool tc_fused_supported(const flyai_moe_desc& d, int M, bool ep) {
-  return M >= 1 && M < kTcPrefillMinTokens && M * d.top_k <= kTcFusedMaxPairs &&
+  return d.gating == FLYAI_GATE_SOFTMAX_TOPK && M >= 1 && M < kTcPrefillMinTokens && M * d.top_k <= kTcFusedMaxPairs &&
          (ep || (d.expert_begin == 0 && d.expert_end == d.num_experts));
 }
 
@@ -1052,6 +1076,7 @@ int launch_tc_forward(const flyai_moe_desc& d, int M, const void* x, const flyai
   prm.kmax = d.hidden > d.inter ? d.hidden : d.inter;
   prm.limit = d.swiglu_limit;
   prm.alpha = d.swiglu_alpha;
+  prm.situ = d.activation == FLYAI_ACT_SITU;
   prm.err = ws.err;
   TcParams::Route& r = prm.rt;
   r.x = static_cast<const uint16_t*>(x);

@@ -1,7 +1,7 @@
 """One registry of this package's levers, comparing "requested" with "observed".
 
 Each drop-in lever (the GPT-OSS mlp, the DeepSeek MoE.forward, the M2.5 stage
-moe) is switched by an environment flag its module parses at import.  Two facts
+moe, the K3 moe_infer) is switched by an environment flag its module parses at import.  Two facts
 are kept per lever and compared, as the reference's lever registry does
 (engines/deepseek_v4/v4_levers.py:1-40):
 
@@ -20,7 +20,7 @@ finding.
 """
 import os
 
-from . import deepseek, gpt_oss, m25
+from . import deepseek, gpt_oss, k3, m25
 
 # flags read by the shared library or the tools rather than by a lever
 _OTHER_FLAGS = {"FLYAI_MOE_CHECK", "FLYAI_MOE_LEVERS_STRICT"}
@@ -35,6 +35,8 @@ def _levers():
                                deepseek.attempts, lambda: len(deepseek.installed()) > 0),
         "FLYAI_MOE_M25": ("minimax-m2.5 stage moe", lambda: m25.ENABLED,
                           m25.attempts, lambda: len(m25.installed()) > 0),
+        "FLYAI_MOE_K3": ("kimi-k3 moe_infer", lambda: k3.ENABLED,
+                         k3.attempts, lambda: len(k3.installed()) > 0),
     }
 
 

@@ -37,6 +37,12 @@ M25 = dict(num_experts=256, top_k=8, hidden=3072, inter=1536)
 # dim 4096, moe_inter_dim 2048, 256 routed experts (fp4), 6 active, 1 shared
 # expert (fp8), sqrtsoftplus scores, route_scale 1.5, swiglu_limit 10.
 V4 = dict(num_experts=256, top_k=6, hidden=4096, inter=2048, route_scale=1.5, swiglu_limit=10.0)
+# Kimi-K3 routed experts behind moe_infer: 896 MXFP4 experts per layer
+# (engines/kimi_k3/k3_moe_mxfp4.py:260), top-16 (the probe router of its
+# docstring), situ beta 4 / linear_beta 25 (the configuration
+# engines/kimi_k3/k3_pipe.py:747 builds).  The latent expert width and the expert
+# intermediate size are not in the reference tree: 2048 and 1024 stand in.
+K3 = dict(num_experts=896, top_k=16, hidden=2048, inter=1024, beta=4.0, linear_beta=25.0)
 # The fp8 weights [N, K] a DeepSeek-V4-Flash decode layer multiplies one token
 # row by (engines/deepseek_v4/v4_fp8_gemv.py:10-14): attention, the ratio-4
 # layers' indexer wq_b, and the shared expert (w1 and w3 read the same x).
@@ -281,3 +287,50 @@ def make_fp8_linear(N, K, seed=0, e8m0=True, device="cpu"):
     else:
         s = torch.exp(torch.randn(N // 128, K // 128, **rnd) * 0.5 - 6.0)
     return w, s
+
+
+@dataclass
+class K3Layer:
+    """Seeded Kimi-K3 MXFP4 experts (the checkpoint's ``mxfp4-pack-quantized``
+    tensors, engines/kimi_k3/k3_moe_mxfp4.py:326-340): ``expert(e)`` -> (w1 uint8
+    [I, H/2], s1 uint8 [I, H/32], w3, s3 alike, w2 uint8 [H, I/2], s2 uint8
+    [H, I/32]): e2m1 nibbles uniform over all 16 codes (low nibble = even K), e8m0
+    exponents uniform in [118, 124]; each expert has its own generator seed.
+    ``routing(M)`` -> (topk_ids int64 [M, k], k distinct experts per token;
+    topk_weight fp32 [M, k], positive, summing to 1 per token) standing in for
+    KimiMoEGate's output."""
+    num_experts: int
+    top_k: int
+    hidden: int
+    inter: int
+    beta: float
+    linear_beta: float
+    seed: int
+    device: str = "cpu"
+
+    def expert(self, e, device=None):
+        device = device or self.device
+        g = torch.Generator(device=device).manual_seed(self.seed * 1_000_003 + 7_368_787 * (e + 1))
+        rnd = dict(generator=g, device=device)
+        H, I = self.hidden, self.inter
+        w1 = torch.randint(0, 256, (I, H // 2), dtype=torch.uint8, **rnd)
+        s1 = torch.randint(118, 125, (I, H // 32), dtype=torch.uint8, **rnd)
+        w3 = torch.randint(0, 256, (I, H // 2), dtype=torch.uint8, **rnd)
+        s3 = torch.randint(118, 125, (I, H // 32), dtype=torch.uint8, **rnd)
+        w2 = torch.randint(0, 256, (H, I // 2), dtype=torch.uint8, **rnd)
+        s2 = torch.randint(118, 125, (H, I // 32), dtype=torch.uint8, **rnd)
+        return w1, s1, w3, s3, w2, s2
+
+    def routing(self, num_tokens, seed=0, device=None):
+        device = device or self.device
+        g = torch.Generator(device="cpu").manual_seed(self.seed * 7919 + seed + 17)
+        ids = torch.stack([torch.randperm(self.num_experts, generator=g)[:self.top_k]
+                           for _ in range(num_tokens)]) if num_tokens else \
+            torch.zeros(0, self.top_k, dtype=torch.long)
+        w = torch.rand(num_tokens, self.top_k, generator=g) + 0.05
+        w = w / w.sum(-1, keepdim=True)
+        return ids.to(device), w.float().to(device)
+
+
+def make_k3_layer(num_experts, top_k, hidden, inter, beta=4.0, linear_beta=25.0, seed=0, device="cpu"):
+    return K3Layer(num_experts, top_k, hidden, inter, beta, linear_beta, seed, str(device))

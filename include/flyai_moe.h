@@ -19,7 +19,10 @@
  *   - MoE.forward / Gate.forward / Expert.forward of the DeepSeek reference
  *       vendor/deepseek_v4_ref/inference/model.py:569-649;
  *   - KimiMoEGate.forward (DeepSeek-V3 grouped sigmoid gate)
- *       vendor/kimi_k3_ref/modeling_kimi_linear.py:703-759.
+ *       vendor/kimi_k3_ref/modeling_kimi_linear.py:703-759;
+ *   - KimiSparseMoeBlock.moe_infer (Kimi-K3 MXFP4 experts with `situ`)
+ *       vendor/kimi_k3_ref/modeling_kimi_linear.py:841-875, served on the GPU by
+ *       engines/kimi_k3/k3_moe_mxfp4.py:258-412.
  */
 #ifndef FLYAI_MOE_H
 #define FLYAI_MOE_H
@@ -79,6 +82,11 @@ extern "C" {
                                        (sorted; torch's CPU order among ties) -- or tid2eid[input_ids] on
                                        a hash-routed layer (flyai_moe_route_hash) --, the unbiased scores
                                        / their sum x route_scale; router_b = fp32 [E], weights fp32 */
+#define FLYAI_GATE_EXTERNAL      5  /* Kimi-K3: the caller's router chose the experts -- the seam is
+                                       moe_infer(x, topk_ids, topk_weight) (engines/kimi_k3/
+                                       k3_moe_mxfp4.py:405-412, vendor/kimi_k3_ref/modeling_kimi_linear.py:
+                                       841-875), ids and weights from its KimiMoEGate; they enter through
+                                       flyai_moe_route_ids.  MXFP4 with FLYAI_ACT_SITU only */
 
 /* expert activations */
 #define FLYAI_ACT_GPTOSS_SWIGLU  1  /* interleaved gate/up, clamp(limit), gate*sigmoid(alpha*gate)*(up+1) */
@@ -87,6 +95,14 @@ extern "C" {
 #define FLYAI_ACT_SILU_BF16      3  /* gate rows [0,I), up rows [I,2I): bf16 silu(gate) * up, down, then
                                        x routing weight (fp32) to bf16, bf16 index_add in ascending
                                        expert id (modeling_minimax_m2.py MiniMaxM2Experts.forward) */
+#define FLYAI_ACT_SITU           4  /* Kimi-K3 `situ` (modeling_kimi_linear.py:64-80, 242-268): w1 (gate)
+                                       and w3 (up) rows as bf16 Linear outputs, in fp32
+                                       beta*tanh(g/beta)*sigmoid(g) * linear_beta*tanh(u/linear_beta) (u
+                                       alone when linear_beta is 0), to bf16; w2 to bf16; the fold is the
+                                       fp32 sum over the k slots in slot order of row x routing weight, to
+                                       bf16 (moe_infer, :841-875).  swiglu_alpha = beta (> 0),
+                                       swiglu_limit = linear_beta (>= 0); W13 blocks are [w1; w3]; top_k
+                                       up to 16; max_tokens up to 64 (larger batches in 64-token calls) */
 
 /* which projection a packed bank holds */
 #define FLYAI_PROJ_W13           0  /* gate/up: rows = 2*inter (interleaved gate,up), K = hidden */
@@ -107,8 +123,8 @@ typedef struct flyai_moe_desc {
                           /*   <= 64 for FP8_BLOCK and FP4_W4A8, <= 8192 for NVFP4      */
                           /*   (calls above 64 tokens take its prefill kernels), any    */
                           /*   for MXFP4                                                */
-  float swiglu_limit;     /* GPT-OSS 7.0 (FLYAI_ACT_SILU: 0 = no clamp)                */
-  float swiglu_alpha;     /* GPT-OSS 1.702 (FLYAI_ACT_SILU: unused, 0)                 */
+  float swiglu_limit;     /* GPT-OSS 7.0 (FLYAI_ACT_SILU: 0 = no clamp; SITU: linear_beta) */
+  float swiglu_alpha;     /* GPT-OSS 1.702 (FLYAI_ACT_SILU: unused, 0; SITU: beta)       */
   int32_t n_group;        /* FLYAI_GATE_SIGMOID_GROUP: expert groups (1 = ungrouped)   */
   int32_t topk_group;     /*   groups kept, 1..n_group                                 */
   float route_scale;      /*   routed_scaling_factor (DeepSeek-V3 2.5)                 */
@@ -144,6 +160,8 @@ FLYAI_API int flyai_moe_packed_bytes(const flyai_moe_desc* desc, int32_t proj, s
 
 /* Load-time relayout of the reference's MXFP4 storage into the kernel bank.
  * blocks: uint8 [E, R, K/32, 16]; scales: uint8 [E, R, K/32]; packed: flyai_moe_packed_bytes.
+ * W13 rows: GPT-OSS's interleaved gate_up_proj; FLYAI_ACT_SITU: w1's rows then w3's (the
+ * checkpoint's weight_packed / weight_scale of each, e2m1 low nibble first, e8m0 per 32).
  * Replaces the reference's load-time handling of the same tensors
  * (transformers/integrations/mxfp4.py:279-330 dequantises them instead). */
 FLYAI_API int flyai_moe_pack_mxfp4(const flyai_moe_desc* desc, int32_t proj, const void* blocks,
@@ -233,6 +251,16 @@ FLYAI_API int flyai_moe_route_logits(const flyai_moe_desc* desc, int32_t num_tok
                                      const void* router_logits, const flyai_moe_weights* w,
                                      int32_t* topk_ids, void* topk_weights, void* workspace,
                                      size_t workspace_bytes, void* stream);
+
+/* Routing chosen by the caller (FLYAI_GATE_EXTERNAL): topk_ids int32 [M, k] and
+ * topk_weights fp32 [M, k] (device) as the reference's gate returned them -- the
+ * moe_infer(x, topk_ids, topk_weight) seam of Kimi-K3 (engines/kimi_k3/
+ * k3_moe_mxfp4.py:405-412).  Leaves the ids, weights, expert histogram and stable
+ * permutation in the workspace for flyai_moe_experts (or _experts_pairs).  An id
+ * outside [0, E) is read as 0 and sets bit 2 of the error word. */
+FLYAI_API int flyai_moe_route_ids(const flyai_moe_desc* desc, int32_t num_tokens,
+                                  const int32_t* topk_ids, const float* topk_weights,
+                                  void* workspace, size_t workspace_bytes, void* stream);
 
 /* Copy the routing plan flyai_moe_route left in the workspace: counts (int32
  * [El]) and exclusive offsets (int32 [El+1]) of this shard's experts, and the
