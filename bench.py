@@ -10,7 +10,8 @@ this host.  At N=1 the line also carries "families": the DeepSeek-V3 FP8 layer
 (config 3), the MiniMax-M2.5 NVFP4 layer (config 4, with its M=4096 prefill) and
 the DeepSeek-V4-Flash W4A8 layer, each with its verify-size sweep, expert-kernel
 roofline, end-to-end time and CPU oracle timing, and "linear": the seven dense
-FP8 GEMMs of a DeepSeek-V4-Flash decode layer (flyai_fp8_linear).
+FP8 GEMMs of a DeepSeek-V4-Flash decode layer (flyai_fp8_linear), and "k3": the
+Kimi-K3 routed experts behind moe_infer (caller-routed MXFP4 with situ).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
@@ -91,6 +92,8 @@ def parse():
                         "write then a 256 MiB read (its write-backs finish before the step)")
     p.add_argument("--no-linear", action="store_true",
                    help="default run: leave out the dense FP8 linear sub-object")
+    p.add_argument("--no-k3", action="store_true",
+                   help="default run: leave out the Kimi-K3 moe_infer sub-object")
     return p.parse_args()
 
 
@@ -470,6 +473,8 @@ def main():
         result["families"] = fam
     if world == 1 and not args.no_linear:
         result["linear"] = linear_result(args, dev, flush)
+    if world == 1 and not args.no_k3:
+        result["k3"] = k3_result(args, dev, flush)
     if rank == 0:
         print(json.dumps(result), flush=True)
     if ep is not None:
@@ -839,6 +844,90 @@ def linear_result(args, dev, flush):
             "weight_bytes_per_layer": total_bytes, "l2": flush.note,
             "data": "synthetic (seeded N(0,1) e4m3 weights, e8m0 scales 2^-10..2^-7, bf16 N(0,1) x)",
             **out}
+
+
+def k3_result(args, dev, flush):
+    """Kimi-K3 routed experts behind moe_infer (synth.K3: 896 MXFP4 experts, top-16,
+    latent 2048, intermediate 1024, situ beta 4 / linear_beta 25), routing given by
+    the caller: microseconds per moe_infer call at M = 1, 8, 64 (L2 flushed before
+    each), the expert kernel alone, its HBM roofline on the distinct experts'
+    MXFP4 bytes, and the CPU oracle on the host at M=1 (weights dequantised once,
+    untimed)."""
+    from flyai_b200.k3 import K3MoE
+    from flyai_b200.moe import launch_count, set_profile_events
+    from oracle import k3 as ok3
+    from oracle.v4 import dequant_fp4
+    layer = synth.make_k3_layer(**synth.K3, seed=args.seed, device=dev)
+    moe = K3MoE.from_layer(layer, max_tokens=64, device=dev)
+    hbm_peak, peak_kind = peaks()
+    per_expert = ok3.expert_bytes(layer.hidden, layer.inter)
+    out = {"workload": "Kimi-K3 routed experts (moe_infer): E=896 MXFP4, top-16, H=2048 (latent), "
+                       "I=1024, situ", "l2": flush.note,
+           "data": "synthetic (seeded e2m1 nibbles, e8m0 2^-9..2^-3, bf16 N(0,1) x, random top-16 "
+                   "routing with positive weights)"}
+    for M in (1, 8, 64):
+        x = synth.make_tokens(M, layer.hidden, seed=args.seed, device=dev)
+        ids, wts = layer.routing(M, seed=M, device=dev)
+        y = torch.empty(M, layer.hidden, dtype=torch.bfloat16, device=dev)
+        for _ in range(args.warmup):
+            flush()
+            moe.moe_infer(x, ids, wts, out=y)
+        torch.cuda.synchronize()
+        steps = args.steps
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(steps)]
+        n0 = launch_count()
+        for (a, b), (ka, kb) in zip(ev, kev):
+            flush()
+            set_profile_events(ka, kb)
+            a.record()
+            moe.moe_infer(x, ids, wts, out=y)
+            b.record()
+        set_profile_events(None, None)
+        torch.cuda.synchronize()
+        launches = (launch_count() - n0) // steps
+        ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+        kms = sum(a.elapsed_time(b) for a, b in kev) / steps
+        distinct = int(torch.unique(ids).numel())
+        nbytes = distinct * per_expert
+        gbs = nbytes / (kms * 1e-3) / 1e9
+        out[f"M{M}"] = {"us": round(ms * 1e3, 2), "kernel_us": round(kms * 1e3, 2),
+                        "gpu_launches": launches, "distinct_experts": distinct,
+                        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak,
+                                     "unit": "GB/s", "frac": round(gbs / hbm_peak, 4),
+                                     "peak_source": peak_kind, "bytes_per_launch": nbytes,
+                                     "kernel": "tc_moe_kernel<false> (situ gate/up + down)"}}
+        assert moe.read_error()[0] == 0
+    # CPU oracle at M=1 on the host cores (the touched experts dequantised untimed)
+    x = synth.make_tokens(1, layer.hidden, seed=args.seed)
+    ids, wts = layer.routing(1, seed=1, device="cpu")
+    deq = {}
+    for e in sorted(set(int(v) for v in ids.ravel())):
+        w1, s1, w3, s3, w2, s2 = (t.cpu().numpy() for t in layer.expert(e))
+        deq[e] = (dequant_fp4(w1, s1), dequant_fp4(w3, s3), dequant_fp4(w2, s2))
+    xn, idn, wn = x.float().numpy(), ids.numpy(), wts.numpy()
+
+    def cpu_call():
+        rows = np.zeros((1, layer.top_k, layer.hidden), np.float32)
+        for s_, e in enumerate(idn[0]):
+            W1, W3, W2 = deq[int(e)]
+            g = ok3.round_bf16((xn @ W1.T).astype(np.float32))
+            u = ok3.round_bf16((xn @ W3.T).astype(np.float32))
+            h = ok3.situ(g, u, layer.beta, layer.linear_beta)
+            rows[:, s_] = ok3.round_bf16((h @ W2.T).astype(np.float32))
+        acc = rows[:, 0] * wn[:, 0:1]
+        for s_ in range(1, layer.top_k):
+            acc = (acc + rows[:, s_] * wn[:, s_:s_ + 1]).astype(np.float32)
+        return ok3.round_bf16(acc)
+    t, n, spread = time_cpu(cpu_call, budget_s=10.0)
+    out["cpu_baseline"] = {"value": round(t * 1e6, 1), "unit": "us", "cores": torch.get_num_threads(),
+                           "kind": "port", "statistic": "median", **cpu_spread_us(spread),
+                           "sample": f"{n} moe_infer calls at M=1 (16 experts; dequantised once, untimed)"}
+    del moe
+    torch.cuda.empty_cache()
+    return out
 
 
 def m25_prefill(args, layer, erange, world, dev, flush, max_over_ranks, hbm_peak):
