@@ -48,7 +48,7 @@ EXPORTS = (
     "flyai_moe_experts_ep", "flyai_moe_combine_ep", "flyai_moe_forward_ep",
     "flyai_moe_forward_noalloc", "flyai_moe_read_error", "flyai_moe_pack_fp8",
     "flyai_moe_pack_nvfp4", "flyai_moe_pack_nvfp4_swizzled", "flyai_moe_pack_fp4", "flyai_moe_pack_shared_fp8",
-    "flyai_moe_route_hash", "flyai_moe_route_logits", "flyai_moe_route_ids",
+    "flyai_moe_route_hash", "flyai_moe_route_logits", "flyai_moe_route_ids", "flyai_moe_experts_slots",
     "flyai_fp8_linear_bank_bytes", "flyai_fp8_linear_pack", "flyai_fp8_linear_workspace_bytes",
     "flyai_fp8_linear",
 )
@@ -141,6 +141,7 @@ def load():
         "flyai_moe_route_hash": ([pd, i32, vp, vp, vp, i32, pw, vp, vp, vp, vp, sz, vp], ctypes.c_int),
         "flyai_moe_route_logits": ([pd, i32, vp, vp, pw, vp, vp, vp, sz, vp], ctypes.c_int),
         "flyai_moe_route_ids": ([pd, i32, vp, vp, vp, sz, vp], ctypes.c_int),
+        "flyai_moe_experts_slots": ([pd, i32, vp, pw, vp, i32, vp, vp, sz, vp], ctypes.c_int),
         "flyai_moe_workspace_bytes": ([pd, ctypes.POINTER(sz)], ctypes.c_int),
         "flyai_moe_route": ([pd, i32, vp, pw, vp, vp, vp, vp, sz, vp], ctypes.c_int),
         "flyai_moe_experts": ([pd, i32, vp, pw, vp, vp, sz, vp], ctypes.c_int),

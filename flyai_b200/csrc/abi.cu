@@ -485,6 +485,24 @@ int flyai_moe_experts(const flyai_moe_desc* desc, int32_t M, const void* x,
   return folded ? FLYAI_OK : launch_combine(*desc, M, ws.pair_out, y, ws, s);
 }
 
+int flyai_moe_experts_slots(const flyai_moe_desc* desc, int32_t M, const void* x,
+                            const flyai_moe_weights* w, const int32_t* slot_of, int32_t slots,
+                            void* y, void* workspace, size_t workspace_bytes, void* stream) {
+  FLYAI_TRY(check_desc(desc));
+  if (desc->format != FLYAI_FMT_FP4_W4A8) return FLYAI_ERR_UNSUPPORTED;
+  FLYAI_TRY(check_tokens(desc, M));
+  FLYAI_TRY(check_workspace(desc, workspace, workspace_bytes));
+  FLYAI_TRY(check_weights(desc, w, false, true));
+  FLYAI_TRY(check_fp8_compute(*desc));
+  if (slots < 1 || !slot_of) return FLYAI_ERR_INVALID_ARG;
+  if (M > 0 && (!x || !y)) return FLYAI_ERR_INVALID_ARG;
+  if ((x && !aligned(x, 16)) || (y && !aligned(y, 16)) || !aligned(slot_of, 4))
+    return FLYAI_ERR_ALIGNMENT;
+  const Fp8Workspace fw = carve_fp8_workspace(*desc, desc->max_tokens, workspace);
+  return launch_v4_experts(*desc, M, *w, y, fw.rows, fw, static_cast<cudaStream_t>(stream),
+                           g_prof_start.load(), g_prof_stop.load(), slot_of, slots);
+}
+
 int flyai_moe_forward(const flyai_moe_desc* desc, int32_t M, const void* x,
                       const flyai_moe_weights* w, void* y, int32_t* topk_ids,
                       void* topk_weights, void* workspace, size_t workspace_bytes,

@@ -216,9 +216,11 @@ int launch_v4_pack_fp4(const flyai_moe_desc& d, int proj, const void* blocks, co
                        void* packed, cudaStream_t stream);
 int launch_v4_pack_shared(const flyai_moe_desc& d, int proj, const void* weight, const void* scale,
                           void* packed, cudaStream_t stream);
+// slot_of != null: the bank is an expert cache of `slots` routed experts then the
+// shared expert; routed expert e (local index) sits in slot slot_of[e].
 int launch_v4_experts(const flyai_moe_desc& d, int M, const flyai_moe_weights& w, void* y,
                       uint16_t* rows, const Fp8Workspace& ws, cudaStream_t stream, cudaEvent_t ev0,
-                      cudaEvent_t ev1);
+                      cudaEvent_t ev1, const int32_t* slot_of = nullptr, int slots = 0);
 // Rows of the pair-row buffer of a batch of M tokens.
 inline size_t layer_pair_rows(const flyai_moe_desc& d, int M) {
   return static_cast<size_t>(M) * (d.top_k + d.n_shared);

@@ -264,6 +264,10 @@ struct V4Params {
   int H, P;
   float limit;
   int32_t* err;
+  // expert cache (slots > 0): routed expert e of the plan is read from slot
+  // slot_of[e]; the shared expert follows the `slots` routed slots
+  const int32_t* slot_of;
+  int slots;
 };
 
 __host__ __device__ inline size_t v4_smem_bytes() {
@@ -367,9 +371,20 @@ __global__ void __launch_bounds__(kV4Threads, 1) v4_moe_kernel(const __grid_cons
         const V4Bank& B = t.gu ? p.b13 : p.b2;
         const bool f8 = e >= p.El;
         const size_t blk = f8 ? B.f8_block : B.fp4_block;
+        int es = e;
+        size_t shared_off = B.shared_off;
+        if (p.slots > 0) {
+          // a slot outside the cache (the host's table is wrong) reads slot 0, recorded
+          es = f8 ? 0 : __ldg(&p.slot_of[e]);
+          if (es < 0 || es >= p.slots) {
+            atomicOr(p.err, kErrBadIndex);
+            es = 0;
+          }
+          shared_off = static_cast<size_t>(p.slots) * B.fp4_expert;
+        }
         const uint8_t* a = (t.gu ? p.w13 : p.w2) +
-                           (f8 ? B.shared_off + static_cast<size_t>(e - p.El) * B.f8_expert
-                               : static_cast<size_t>(e) * B.fp4_expert) +
+                           (f8 ? shared_off + static_cast<size_t>(e - p.El) * B.f8_expert
+                               : static_cast<size_t>(es) * B.fp4_expert) +
                            static_cast<size_t>(t.mt) * B.KB * blk;
         const uint8_t* b = (t.gu ? p.xb : p.hb) + static_cast<size_t>(t.chunk) * B.KB * kV4BBytes;
         const uint32_t abytes = static_cast<uint32_t>(blk);
@@ -632,7 +647,7 @@ __global__ void __launch_bounds__(kV4Threads, 1) v4_moe_kernel(const __grid_cons
 
 int launch_v4_experts(const flyai_moe_desc& d, int M, const flyai_moe_weights& w, void* y,
                       uint16_t* rows, const Fp8Workspace& ws, cudaStream_t stream, cudaEvent_t ev0,
-                      cudaEvent_t ev1) {
+                      cudaEvent_t ev1, const int32_t* slot_of, int slots) {
   if (M == 0) return FLYAI_OK;
   const int P = M * d.top_k;
   V4ScatterParams sp{ws.xq, ws.xs, ws.perm, ws.n_chunks, ws.chunk_info, ws.xb, d.hidden, d.top_k, P};
@@ -668,6 +683,8 @@ int launch_v4_experts(const flyai_moe_desc& d, int M, const flyai_moe_weights& w
   prm.P = P;
   prm.limit = d.swiglu_limit;
   prm.err = ws.err;
+  prm.slot_of = slot_of;
+  prm.slots = slot_of ? slots : 0;
   if (ev0 && ev1 && cudaEventRecord(ev0, stream) != cudaSuccess) return FLYAI_ERR_CUDA;
   if (v4_launch(v4_moe_kernel, dim3(sms), kV4Threads, smem, stream, true, prm) != cudaSuccess)
     return FLYAI_ERR_CUDA;

@@ -262,6 +262,22 @@ FLYAI_API int flyai_moe_route_ids(const flyai_moe_desc* desc, int32_t num_tokens
                                   const int32_t* topk_ids, const float* topk_weights,
                                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* DeepSeek-V4 routed experts from an expert cache (the reference's RAM expert
+ * tier, engines/deepseek_v4/v4_hybrid.py:113-160 / v4_expert_cache.py: the routed
+ * experts live in host memory and only a fixed set of device slots holds weights).
+ * FLYAI_FMT_FP4_W4A8 only; as flyai_moe_experts after flyai_moe_route /
+ * flyai_moe_route_hash, but w->w13 / w->w2 are cache banks laid out as the bank of
+ * a descriptor whose expert range holds `slots` experts (flyai_moe_packed_bytes of
+ * that descriptor): slot s at s times one expert's packed bytes, the shared expert
+ * after the last slot.  slot_of (int32 [expert_end - expert_begin], device) gives
+ * the slot of every routed expert; every expert the routing picked must be in a
+ * slot (one that is not, or a slot outside [0, slots), reads slot 0 and sets bit 2
+ * of the error word).  Output identical to flyai_moe_experts on the full bank. */
+FLYAI_API int flyai_moe_experts_slots(const flyai_moe_desc* desc, int32_t num_tokens, const void* x,
+                                      const flyai_moe_weights* w, const int32_t* slot_of,
+                                      int32_t slots, void* y, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+
 /* Copy the routing plan flyai_moe_route left in the workspace: counts (int32
  * [El]) and exclusive offsets (int32 [El+1]) of this shard's experts, and the
  * permutation (int32 [M*k]): position p holds the flat pair index token*k+slot,
