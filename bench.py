@@ -92,6 +92,10 @@ def parse():
                         "write then a 256 MiB read (its write-backs finish before the step)")
     p.add_argument("--no-linear", action="store_true",
                    help="default run: leave out the dense FP8 linear sub-object")
+    p.add_argument("--ep-prefill", default="replicated", choices=["replicated", "tokens"],
+                   help="N>1 prefill leg: every rank routes all tokens and the pair rows are "
+                        "all-reduced (default), or tokens sharded by rank with rows sent to "
+                        "their expert's owner by NCCL all-to-all")
     p.add_argument("--no-k3", action="store_true",
                    help="default run: leave out the Kimi-K3 moe_infer sub-object")
     return p.parse_args()
@@ -440,7 +444,21 @@ def main():
         xp = synth.make_tokens(MP, H, seed=args.seed + 1, device=dev)
         yp = torch.empty(MP, H, dtype=torch.bfloat16, device=dev)
         psteps = max(3, min(args.steps, 10))
-        pms, _ = timed(lambda: layer_step(xp, yp), psteps, max(3, min(args.warmup, 3)))
+        pmode = "single GPU"
+        if world > 1 and args.ep_prefill == "replicated":
+            pms, _ = timed(lambda: layer_step(xp, yp), psteps, max(3, min(args.warmup, 3)))
+            pmode = f"tokens replicated on {world} ranks, pair rows all-reduced"
+        elif world > 1:
+            # tokens sharded by rank: each routes its MP/N tokens, rows travel to their
+            # expert's owner and back over NCCL all-to-all (flyai_b200.ep.TokenShardedMoE)
+            from flyai_b200.ep import PairExperts, TokenShardedMoE
+            tsm = TokenShardedMoE(moe, PairExperts(moe, max_rows=4096))
+            a, b = rank * MP // world, (rank + 1) * MP // world
+            xl, yl = xp[a:b].contiguous(), yp[a:b]
+            pms, _ = timed(lambda: tsm.forward(xl, yl), psteps, max(3, min(args.warmup, 3)))
+            pmode = f"tokens sharded over {world} ranks, rows to their expert's owner by NCCL all-to-all"
+        else:
+            pms, _ = timed(lambda: layer_step(xp, yp), psteps, max(3, min(args.warmup, 3)))
         _, pids, _ = moe.route(xp, logits=False)
         torch.cuda.synchronize()
         pb, pdist, _ = touched_bytes(pids)
@@ -451,7 +469,8 @@ def main():
                              "hbm_frac": round(pb / (pms * 1e-3) / 1e9 / world / hbm_peak, 4),
                              "tflops": round(flops / (pms * 1e-3) / 1e12, 2),
                              "distinct_experts": pdist,
-                             "max_expert_load": int(load.max()), "steps": psteps}
+                             "max_expert_load": int(load.max()), "steps": psteps,
+                             "parallelism": pmode}
         moe.router_b.copy_(layer.router_b)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

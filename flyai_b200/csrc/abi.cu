@@ -39,10 +39,12 @@ static int check_desc(const flyai_moe_desc* d) {
     return FLYAI_ERR_INVALID_ARG;
   if (d->max_tokens < 0) return FLYAI_ERR_INVALID_ARG;
   if (d->format == FLYAI_FMT_MXFP4) {
-    // GPT-OSS (routed here, SwiGLU) or Kimi-K3 (routed by the caller, situ)
-    const bool k3 = d->gating == FLYAI_GATE_EXTERNAL;
-    if (!k3 && d->gating != FLYAI_GATE_SOFTMAX_TOPK) return FLYAI_ERR_UNSUPPORTED;
-    if (d->activation != (k3 ? FLYAI_ACT_SITU : FLYAI_ACT_GPTOSS_SWIGLU)) return FLYAI_ERR_UNSUPPORTED;
+    // GPT-OSS (SwiGLU) routed here, or routed by the caller (token-sharded expert
+    // parallel: the pairs another rank sent); Kimi-K3 (situ, routed by the caller)
+    const bool ext = d->gating == FLYAI_GATE_EXTERNAL;
+    const bool k3 = ext && d->activation == FLYAI_ACT_SITU;
+    if (!ext && d->gating != FLYAI_GATE_SOFTMAX_TOPK) return FLYAI_ERR_UNSUPPORTED;
+    if (!k3 && d->activation != FLYAI_ACT_GPTOSS_SWIGLU) return FLYAI_ERR_UNSUPPORTED;
     // the tcgen05 kernels: K-tiles of 64, one tensor-memory accumulator row block
     if (d->hidden % 64 || d->inter % 64) return FLYAI_ERR_ALIGNMENT;
     if (d->hidden > kTcMaxK || d->inter > kTcMaxK) return FLYAI_ERR_UNSUPPORTED;

@@ -144,3 +144,94 @@ class ExpertParallelMoE:
             self._pairs = torch.empty(max(need, 1), self.shard.hidden, dtype=torch.bfloat16,
                                       device=x.device)
         return self._pairs[:need]
+
+
+class PairExperts:
+    """A shard's experts applied to (token row, expert, routing weight) triples
+    that other ranks sent: the shard's banks under an MXFP4 descriptor with caller
+    routing (FLYAI_GATE_EXTERNAL) and one slot per row.  ``run`` returns the
+    weighted bf16 rows, computed as the shard's own pair rows are."""
+
+    def __init__(self, shard, max_rows=4096):
+        self.shard = shard
+        self.max_rows = max_rows
+        self.desc = _lib.Desc.from_buffer_copy(shard.desc)
+        self.desc.gating = _lib.GATE_EXTERNAL
+        self.desc.top_k = 1
+        self.desc.max_tokens = max_rows
+        _lib.call("flyai_moe_check_desc", ctypes.byref(self.desc))
+        nbytes = ctypes.c_size_t()
+        _lib.call("flyai_moe_workspace_bytes", ctypes.byref(self.desc), ctypes.byref(nbytes))
+        self.workspace = torch.zeros(nbytes.value, dtype=torch.uint8, device=shard.device)
+
+    def run(self, rows, ids, wts, out=None):
+        """rows bf16 [R, H]; ids int32 [R] (experts of this shard); wts fp32 [R]."""
+        from .moe import _ptr, _stream
+        R = rows.shape[0]
+        out = out if out is not None else torch.empty_like(rows)
+        ws = self.workspace
+        with torch.cuda.device(self.shard.device):
+            for r0 in range(0, R, self.max_rows):
+                m = min(self.max_rows, R - r0)
+                _lib.call("flyai_moe_route_ids", ctypes.byref(self.desc), m, _ptr(ids[r0:r0 + m]),
+                          _ptr(wts[r0:r0 + m]), _ptr(ws), ws.numel(), _stream())
+                _lib.call("flyai_moe_experts_pairs", ctypes.byref(self.desc), m, _ptr(rows[r0:r0 + m]),
+                          ctypes.byref(self.shard.weights), _ptr(out[r0:r0 + m]), _ptr(ws), ws.numel(),
+                          _stream())
+        return out
+
+
+class TokenShardedMoE:
+    """Expert parallel with the tokens sharded by rank (prefill): each rank routes
+    its own tokens over all experts, sends each (token, slot) pair's token row to
+    the rank owning the expert (NCCL all-to-all, counts first), the owners compute
+    the weighted rows (``pairs.run``) and send them back, and each rank folds its
+    tokens' k rows with the layer's own combine -- every row crosses the links
+    once each way, where the replicated path all-reduces the whole [M*k, H] pair
+    matrix (the expert sharding of vendor/deepseek_v4_ref/inference/model.py:620-647,
+    with each row moved once to its expert's owner instead of an all-reduce).
+    ``shard``: this rank's layer shard (route, combine); ``pairs``: its
+    ``PairExperts``.  Output for a rank's tokens equals the single-GPU layer's."""
+
+    def __init__(self, shard, pairs, group=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.shard, self.pairs, self.group = shard, pairs, group
+        self.world = dist.get_world_size(group)
+
+    def forward(self, x, out=None):
+        """x: this rank's tokens, bf16 [M_r, H] -> y for them."""
+        d, g, W = self.dist, self.group, self.world
+        sh = self.shard
+        M, H, k = x.shape[0], sh.hidden, sh.top_k
+        per = sh.num_experts // W
+        if M > 0:
+            _, ids, wts = sh.route(x, logits=False)
+            ids = torch.as_tensor(ids).to(x.device).reshape(-1).to(torch.int32)
+            wts = torch.as_tensor(wts).to(x.device).reshape(-1).float()
+        else:
+            ids = torch.empty(0, dtype=torch.int32, device=x.device)
+            wts = torch.empty(0, dtype=torch.float32, device=x.device)
+        dest = ids.long() // per
+        order = torch.sort(dest, stable=True).indices          # pairs grouped by owner rank
+        send = torch.bincount(dest, minlength=W).to(torch.int64)
+        recv = torch.empty_like(send)
+        d.all_to_all_single(recv, send, group=g)
+        sc, rc = send.tolist(), recv.tolist()                    # split sizes (host)
+        R = sum(rc)
+        rows_recv = x.new_empty(R, H)
+        d.all_to_all_single(rows_recv, x[order // k].contiguous(), rc, sc, group=g)
+        ids_recv = torch.empty(R, dtype=torch.int32, device=x.device)
+        d.all_to_all_single(ids_recv, ids[order].contiguous(), rc, sc, group=g)
+        wts_recv = torch.empty(R, dtype=torch.float32, device=x.device)
+        d.all_to_all_single(wts_recv, wts[order].contiguous(), rc, sc, group=g)
+        done = self.pairs.run(rows_recv, ids_recv, wts_recv) if R else rows_recv
+        back = x.new_empty(M * k, H)
+        d.all_to_all_single(back, done.contiguous(), sc, rc, group=g)
+        pair_out = x.new_empty(M * k, H)
+        pair_out[order] = back
+        if M == 0:
+            return out if out is not None else x.new_empty(0, H)
+        if out is not None:
+            return sh.combine(pair_out, M, out)
+        return sh.combine(pair_out, M)

@@ -85,8 +85,10 @@ extern "C" {
 #define FLYAI_GATE_EXTERNAL      5  /* Kimi-K3: the caller's router chose the experts -- the seam is
                                        moe_infer(x, topk_ids, topk_weight) (engines/kimi_k3/
                                        k3_moe_mxfp4.py:405-412, vendor/kimi_k3_ref/modeling_kimi_linear.py:
-                                       841-875), ids and weights from its KimiMoEGate; they enter through
-                                       flyai_moe_route_ids.  MXFP4 with FLYAI_ACT_SITU only */
+                                       841-875), ids and weights from its KimiMoEGate -- or, with
+                                       FLYAI_ACT_GPTOSS_SWIGLU, the (row, expert, weight) pairs another
+                                       rank sent for this rank's experts (token-sharded expert parallel);
+                                       they enter through flyai_moe_route_ids.  MXFP4 only */
 
 /* expert activations */
 #define FLYAI_ACT_GPTOSS_SWIGLU  1  /* interleaved gate/up, clamp(limit), gate*sigmoid(alpha*gate)*(up+1) */

@@ -16,7 +16,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from flyai_b200 import synth
-from flyai_b200.ep import ExpertParallelMoE, expert_range
+from flyai_b200.ep import ExpertParallelMoE, TokenShardedMoE, expert_range
 from oracle import gpt_oss as og
 from oracle.fp import round_bf16
 from tests.golden_util import oracle_weights
@@ -30,6 +30,7 @@ class OracleShard:
         self.lo, self.hi = lo, hi
         self.top_k = layer.top_k
         self.hidden = layer.hidden
+        self.num_experts = layer.num_experts
 
     def route(self, x, logits=True):
         _, self.ids, self.wts = og.router(x.float().numpy(), self.w.router_w, self.w.router_b,
@@ -55,6 +56,58 @@ class OracleShard:
             for s in np.argsort(self.ids[t], kind="stable"):   # ascending expert id
                 y[t] = round_bf16(y[t] + r[t, s])
         return torch.from_numpy(y).bfloat16()
+
+
+class OraclePairs:
+    """PairExperts' surface: a shard's experts on (row, expert, weight) triples."""
+
+    def __init__(self, shard):
+        self.shard = shard
+
+    def run(self, rows, ids, wts):
+        xf, ids, wts = rows.float().numpy(), ids.numpy(), wts.numpy()
+        out = np.zeros_like(xf)
+        for e in np.unique(ids):
+            assert self.shard.lo <= e < self.shard.hi   # only this rank's experts arrive
+            r = np.nonzero(ids == e)[0]
+            y, _ = og.expert_forward(xf[r], self.shard.w, int(e))
+            out[r] = round_bf16(y * wts[r][:, None])
+        return torch.from_numpy(out).bfloat16()
+
+
+def _sharded_main(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        layer = synth.make_gpt_oss_layer(num_experts=8, top_k=2, hidden=64, inter=64, seed=5)
+        lo, hi = expert_range(8, world, rank)
+        shard = OracleShard(layer, lo, hi)
+        moe = TokenShardedMoE(shard, OraclePairs(shard))
+        x = synth.make_tokens(7, 64, seed=11)
+        mine = x[:3] if rank == 0 else x[3:]          # uneven token shards
+        q.put((rank, moe.forward(mine).float().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_token_sharded_two_ranks_matches_full_layer():
+    """Each rank routes its own tokens; rows go to the expert owner and back."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sharded_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    got = dict(q.get() for _ in range(world))
+    layer = synth.make_gpt_oss_layer(num_experts=8, top_k=2, hidden=64, inter=64, seed=5)
+    x = synth.make_tokens(7, 64, seed=11)
+    ref = og.moe_forward(x.float().numpy(), oracle_weights(layer), 2)["y"]
+    np.testing.assert_array_equal(np.concatenate([got[0], got[1]]), ref)
 
 
 def _rank_main(rank, world, port, q):
