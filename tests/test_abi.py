@@ -138,3 +138,69 @@ def test_python_layer_refuses_cpu_device():
                  z(4, 128, 2, 16, dtype=torch.uint8), z(4, 128, 2, dtype=torch.uint8), z(4, 128),
                  z(4, 64, 2, 16, dtype=torch.uint8), z(4, 64, 2, dtype=torch.uint8), z(4, 64), 2,
                  device="cpu")
+
+
+def test_caller_routed_and_situ_descriptors():
+    """Kimi-K3 (FLYAI_GATE_EXTERNAL + FLYAI_ACT_SITU) and the token-sharded pair
+    executor (FLYAI_GATE_EXTERNAL + GPT-OSS SwiGLU) validate on the host; the
+    entry points that route themselves refuse caller-routed descriptors before any
+    device work."""
+    lib = _lib.load()
+    k3 = good_desc(gating=_lib.GATE_EXTERNAL, activation=_lib.ACT_SITU, num_experts=896,
+                   expert_end=896, top_k=16, hidden=2048, inter=1024, swiglu_alpha=4.0,
+                   swiglu_limit=25.0)
+    assert lib.flyai_moe_check_desc(ctypes.byref(k3)) == _lib.OK
+    for kw, st in ((dict(top_k=17), _lib.ERR_INVALID_ARG),            # 16 slots at most
+                   (dict(swiglu_alpha=0.0), _lib.ERR_INVALID_ARG),    # beta > 0
+                   (dict(swiglu_limit=-1.0), _lib.ERR_INVALID_ARG),   # linear_beta >= 0 (0 = None)
+                   (dict(swiglu_limit=0.0), _lib.OK),
+                   (dict(max_tokens=65), _lib.ERR_UNSUPPORTED),       # verify kernels only
+                   (dict(activation=_lib.ACT_SILU), _lib.ERR_UNSUPPORTED)):
+        d = _lib.Desc.from_buffer_copy(k3)
+        for k, v in kw.items():
+            setattr(d, k, v)
+        assert lib.flyai_moe_check_desc(ctypes.byref(d)) == st, kw
+    # situ needs caller routing; 16 slots need caller routing
+    assert lib.flyai_moe_check_desc(ctypes.byref(good_desc(activation=_lib.ACT_SITU))) == _lib.ERR_UNSUPPORTED
+    assert lib.flyai_moe_check_desc(ctypes.byref(good_desc(top_k=16))) == _lib.ERR_INVALID_ARG
+    pairs = good_desc(gating=_lib.GATE_EXTERNAL, top_k=1, max_tokens=4096, expert_end=64)
+    assert lib.flyai_moe_check_desc(ctypes.byref(pairs)) == _lib.OK
+    # routing entry points: each takes its own kind of descriptor only
+    assert lib.flyai_moe_forward(ctypes.byref(k3), 1, None, None, None, None, None, None, 0,
+                                 None) == _lib.ERR_UNSUPPORTED
+    assert lib.flyai_moe_route(ctypes.byref(k3), 1, None, None, None, None, None, None, 0,
+                               None) == _lib.ERR_UNSUPPORTED
+    assert lib.flyai_moe_route_ids(ctypes.byref(good_desc()), 1, None, None, None, 0,
+                                   None) == _lib.ERR_UNSUPPORTED
+    assert lib.flyai_moe_route_ids(ctypes.byref(k3), 1, None, None, None, 0,
+                                   None) == _lib.ERR_WORKSPACE
+    # the slot-table experts entry is the V4 layer's
+    assert lib.flyai_moe_experts_slots(ctypes.byref(k3), 1, None, None, None, 4, None, None, 0,
+                                       None) == _lib.ERR_UNSUPPORTED
+
+
+def test_fp8_linear_sizes_and_argument_checks():
+    lib = _lib.load()
+    n = ctypes.c_size_t()
+    # bank: per 128x128 block a 16-byte scale header + the 16 KB tile
+    assert lib.flyai_fp8_linear_bank_bytes(512, 4096, ctypes.byref(n)) == _lib.OK
+    assert n.value == 4 * 32 * (16 + 128 * 128)
+    assert lib.flyai_fp8_linear_bank_bytes(500, 4096, ctypes.byref(n)) == _lib.ERR_ALIGNMENT
+    assert lib.flyai_fp8_linear_bank_bytes(0, 4096, ctypes.byref(n)) == _lib.ERR_INVALID_ARG
+    w1 = ctypes.c_size_t()
+    w64 = ctypes.c_size_t()
+    assert lib.flyai_fp8_linear_workspace_bytes(1, 4096, 8192, ctypes.byref(w1)) == _lib.OK
+    assert lib.flyai_fp8_linear_workspace_bytes(64, 4096, 8192, ctypes.byref(w64)) == _lib.OK
+    assert 0 < w1.value < w64.value
+    big = ctypes.c_size_t()
+    assert lib.flyai_fp8_linear_workspace_bytes(1000, 4096, 8192, ctypes.byref(big)) == _lib.OK
+    assert big.value == w64.value            # one launch holds 64 rows at most
+    assert lib.flyai_fp8_linear_pack(512, 4096, None, None, 0, None, None) == _lib.ERR_INVALID_ARG
+    assert lib.flyai_fp8_linear_pack(512, 4096, None, None, 7, None, None) == _lib.ERR_INVALID_ARG
+    assert lib.flyai_fp8_linear(1, 512, 4096, None, None, 5, None, None, 0, None) == _lib.ERR_INVALID_ARG
+    assert lib.flyai_fp8_linear(0, 512, 4096, None, None, 1, None, None, 0, None) == _lib.OK
+    assert lib.flyai_fp8_linear(1, 512, 4096, ctypes.c_void_p(256), ctypes.c_void_p(256), 1,
+                                ctypes.c_void_p(256), None, 0, None) == _lib.ERR_WORKSPACE
+    assert lib.flyai_fp8_linear(1, 512, 4096, ctypes.c_void_p(256), ctypes.c_void_p(256), 1,
+                                ctypes.c_void_p(256), ctypes.c_void_p(256), 16,
+                                None) == _lib.ERR_WORKSPACE
