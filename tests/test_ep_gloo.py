@@ -11,6 +11,7 @@ import os
 import socket
 
 import numpy as np
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -75,39 +76,47 @@ class OraclePairs:
         return torch.from_numpy(out).bfloat16()
 
 
-def _sharded_main(rank, world, port, q):
+def _sharded_main(rank, world, port, cuts, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
+    y = None
     try:
         layer = synth.make_gpt_oss_layer(num_experts=8, top_k=2, hidden=64, inter=64, seed=5)
         lo, hi = expert_range(8, world, rank)
         shard = OracleShard(layer, lo, hi)
         moe = TokenShardedMoE(shard, OraclePairs(shard))
         x = synth.make_tokens(7, 64, seed=11)
-        mine = x[:3] if rank == 0 else x[3:]          # uneven token shards
-        q.put((rank, moe.forward(mine).float().numpy()))
+        y = moe.forward(x[cuts[rank]:cuts[rank + 1]]).float().numpy()   # uneven, possibly empty
     finally:
+        q.put((rank, y))          # also after a failure, so the parent never waits forever
         dist.destroy_process_group()
 
 
-def test_token_sharded_two_ranks_matches_full_layer():
-    """Each rank routes its own tokens; rows go to the expert owner and back."""
-    world = 2
+@pytest.mark.parametrize("cuts", [(0, 3, 7), (0, 0, 7), (0, 7, 7, 7, 7)])
+def test_token_sharded_ranks_match_full_layer(cuts):
+    """Each rank routes its own tokens (none on some ranks); rows go to the expert
+    owner and back; the ranks' outputs stacked are the full layer's."""
+    world = len(cuts) - 1
     ctx = mp.get_context("spawn")
-    q = ctx.SimpleQueue()
+    q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_sharded_main, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_sharded_main, args=(r, world, port, cuts, q), daemon=True)
+             for r in range(world)]
     for p in procs:
         p.start()
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
-    got = dict(q.get() for _ in range(world))
+    try:
+        got = dict(q.get(timeout=120) for _ in range(world))   # small payloads, read first
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert all(got[r] is not None for r in range(world)), "a rank failed"
     layer = synth.make_gpt_oss_layer(num_experts=8, top_k=2, hidden=64, inter=64, seed=5)
     x = synth.make_tokens(7, 64, seed=11)
     ref = og.moe_forward(x.float().numpy(), oracle_weights(layer), 2)["y"]
-    np.testing.assert_array_equal(np.concatenate([got[0], got[1]]), ref)
+    np.testing.assert_array_equal(np.concatenate([got[r] for r in range(world)]), ref)
 
 
 def _rank_main(rank, world, port, q):
